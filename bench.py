@@ -1,0 +1,609 @@
+"""Benchmark of the B200 per-token layer ops (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mas|reference|flashinfer]
+                    [--workload chain|norm|norm_fp8|silu|rope|embed]
+
+Default workload: configuration 5, the per-layer op chain at 123B-class shapes (H 12288, 96/8 heads,
+D 128, I 28672, V 131072): one step = embed + 88 x (input RMSNorm+residual, rope on q/k, post-attn
+RMSNorm+residual, SiLU-mul on [T, 57344]) over T = 256 decode + 2 x 2048 prefill tokens, with seeded
+random bf16 activations standing in for the attention and GEMM outputs (mas_b200.chain).
+
+Metric: tokens/s of the whole job (all ranks), plus the chain's algorithmic HBM GB/s and its fraction
+of the measured HBM peak. Multi-GPU (torchrun, one rank per GPU) is weak scaling: the global batch is
+N mixed steps and rank r takes the r-th, a contiguous slice; no collective touches the data path.
+NCCL only carries the barrier and the max-over-ranks of the timings (parity of the chain is checked
+by tests/test_gpu_chain.py against the oracle, outside the benchmark).
+
+Reported alongside the device-resident `value`:
+  e2e            the same step through the public API with the step's host inputs (token ids,
+                 positions) copied from pinned memory and the result (the residual stream) read
+                 back, inside the timed region;
+  roofline       the dominant kernel's algorithmic bytes / its CUDA-event time, against the measured
+                 HBM copy peak (MEASURED_PEAKS.json); events bracket each of its launches in the
+                 timed region;
+  cpu_baseline   the C oracle (tests' checker, a restatement of the reference's arithmetic) timed
+                 on this host's cores on a token sample of the same workload (rank 0, N = 1);
+  clocks         SM clock and throttle reasons sampled by nvidia-smi during the timed region.
+
+--impl reference times the reference's CPU path: the reference has no CPU implementation of norm,
+silu or rope (its kernels are flashinfer's, CUDA-only), so this arm runs the C oracle port with all
+host threads on a token sample (embedding included), rank 0 only. --impl flashinfer times the
+reference's actual GPU kernels (flashinfer 0.6.11.post2, aten gather) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Fused-op HBM GB/s (% of B200 peak) and tokens/s at 1/2/4/8 GPUs"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+
+
+def measured_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# --------------------------------------------------------------------------------------------------
+# Process group.
+# --------------------------------------------------------------------------------------------------
+class Dist:
+    def __init__(self, backend: str = "nccl"):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+        if self.world > 1 and backend != "none":
+            import datetime
+
+            import torch.distributed as dist
+
+            if backend == "nccl":
+                torch.cuda.set_device(self.local_rank)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local_rank) if backend == "nccl" else None)
+            self.pg = True
+
+    def barrier(self) -> None:
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, x: float, device) -> float:
+        if not self.pg:
+            return x
+        import torch.distributed as dist
+
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather_objects(self, obj) -> list:
+        if not self.pg:
+            return [obj]
+        import torch.distributed as dist
+
+        out = [None] * self.world
+        dist.all_gather_object(out, obj)
+        return out
+
+    def close(self) -> None:
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+def shard(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous [start, end) slice of `total` units for `rank` (sizes differ by at most one)."""
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+# --------------------------------------------------------------------------------------------------
+# Clock sampling during the timed region.
+# --------------------------------------------------------------------------------------------------
+class Clocks:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, names = [], [], set()
+        reason_names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(reason_names, f[5:9]):
+                if v.lower() == "active":
+                    names.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(names), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------------------------
+# Implementations of the ops (the chain calls whichever namespace it is given).
+# --------------------------------------------------------------------------------------------------
+def mas_ops():
+    import mas_b200
+
+    return mas_b200.ops
+
+
+class FlashinferOps:
+    """The reference's own GPU path: flashinfer kernels and the aten gather behind nn.Embedding."""
+
+    def __init__(self):
+        from flashinfer.activation import silu_and_mul
+        from flashinfer.norm import fused_add_rmsnorm, fused_add_rmsnorm_quant
+        from flashinfer.rope import apply_rope_with_cos_sin_cache_inplace
+
+        self.fused_add_rmsnorm = fused_add_rmsnorm
+        self.fused_add_rmsnorm_quant = fused_add_rmsnorm_quant
+        self.silu_and_mul = silu_and_mul
+        self.apply_rope_with_cos_sin_cache_inplace = apply_rope_with_cos_sin_cache_inplace
+
+    @staticmethod
+    def embedding_out(out, ids, table):
+        return torch.index_select(table, 0, ids, out=out.view(-1, table.shape[1]))
+
+
+# --------------------------------------------------------------------------------------------------
+# Workloads: each builds device state and returns closures for one step.
+# --------------------------------------------------------------------------------------------------
+def chain_config(layers: int, tokens_per_gpu: int, global_tokens: int) -> dict:
+    from mas_b200 import workloads as wl
+
+    s = wl.CHAIN_SHAPE
+    return {"workload": "chain (config 5): embed + 88 x [RMSNorm+res, rope q/k, RMSNorm+res, SiLU-mul]",
+            "hidden": s.hidden_size, "q_heads": s.num_attention_heads, "kv_heads": s.num_key_value_heads,
+            "head_dim": s.head_dim, "intermediate": s.intermediate_size, "vocab": s.vocab_size, "layers": layers,
+            "tokens_per_gpu": tokens_per_gpu, "global_tokens": global_tokens,
+            "step_mix": "256 decode + 2 x 2048 prefill tokens per GPU", "norm": "bf16 fused_add_rmsnorm",
+            "l2": "inputs larger than L2 (per-layer working set 1.84 GB)", "parallelism": "token-sharded dp"}
+
+
+class ChainWorkload:
+    name = "chain"
+    dominant = "fused_add_rmsnorm"
+
+    def __init__(self, device, dist: Dist, ops, layers: int):
+        from mas_b200 import workloads as wl
+        from mas_b200.chain import LayerChain
+
+        self.wl = wl
+        self.shape = wl.CHAIN_SHAPE
+        ids, pos = wl.chain_host_inputs(replicas=dist.world)
+        per = ids.shape[0] // dist.world
+        s, e = dist.rank * per, (dist.rank + 1) * per
+        self.host_ids = ids[s:e].clone().pin_memory()
+        self.host_pos = pos[s:e].clone().pin_memory()
+        self.tokens = per
+        self.global_tokens = ids.shape[0]
+        self.b = wl.chain_buffers(self.host_ids, self.host_pos, device=device, seed=4 + dist.rank, layers=layers)
+        self.chain = LayerChain(self.shape, quant=False, layers=layers)
+        self.chain_ops = ops
+        self.layers = self.chain.layers
+        self.host_out = torch.empty(self.b.residual.shape, dtype=self.b.residual.dtype).pin_memory()
+        self._dom_events = None
+
+    # the chain with a pluggable op namespace, optionally bracketing the dominant kernel with events
+    def _step(self, dom_events=None):
+        b, s, o = self.b, self.shape, self.chain_ops
+        eps = s.rms_norm_eps
+        o.embedding_out(b.hidden, b.ids, b.table)
+        b.residual.zero_()
+        q = b.qkv[:, : s.q_size]
+        k = b.qkv[:, s.q_size: s.q_size + s.kv_size]
+        st = torch.cuda.current_stream()
+        for l in range(self.layers):
+            if dom_events is not None:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+            o.fused_add_rmsnorm(b.hidden, b.residual, b.w_in[l], eps, enable_pdl=True)
+            if dom_events is not None:
+                e1.record(st)
+                dom_events.append((e0, e1))
+            o.apply_rope_with_cos_sin_cache_inplace(b.positions, q, k, s.head_dim, b.cos_sin_cache, is_neox=True)
+            if dom_events is not None:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+            o.fused_add_rmsnorm(b.attn_out, b.residual, b.w_post[l], eps, enable_pdl=True)
+            if dom_events is not None:
+                e1.record(st)
+                dom_events.append((e0, e1))
+            o.silu_and_mul(b.gate_up, out=b.act, enable_pdl=True)
+
+    def step(self, dom_events=None):
+        self._step(dom_events)
+
+    def e2e_step(self):
+        b = self.b
+        b.ids.copy_(self.host_ids, non_blocking=True)
+        b.positions.copy_(self.host_pos, non_blocking=True)
+        self._step(None)
+        self.host_out.copy_(b.residual, non_blocking=True)
+
+    def e2e_bytes(self) -> tuple[int, int]:
+        return (self.host_ids.numel() * 8 + self.host_pos.numel() * 4,
+                self.b.residual.numel() * self.b.residual.element_size())
+
+    def launches_per_step(self) -> int:
+        return 1 + 4 * self.layers
+
+    def step_bytes(self) -> int:
+        return self.chain.step_bytes(self.tokens)
+
+    def dominant_bytes_per_launch(self) -> int:
+        return 8 * self.tokens * self.shape.hidden_size + 2 * self.shape.hidden_size
+
+    def config(self) -> dict:
+        return chain_config(self.layers, self.tokens, self.global_tokens)
+
+
+class OpWorkload:
+    """One op of configurations 1-4 per step (for per-kernel measurements)."""
+
+    def __init__(self, name: str, device, dist: Dist, ops):
+        from mas_b200 import workloads as wl
+
+        self.name, self.o, self.dominant = name, ops, name
+        self.dev = device
+        if name in ("norm", "norm_fp8"):
+            self.x, self.r, self.w, self.eps = wl.norm_inputs(device)
+            self.T, H = self.x.shape
+            self.out = torch.empty(self.x.shape, dtype=torch.float8_e4m3fn, device=device)
+            self.scale = torch.tensor([0.05], device=device)
+            self.bytes = (7 if name == "norm_fp8" else 8) * self.T * H + 2 * H
+            self.cfg = {"workload": f"config 1 {'fp8-out ' if name == 'norm_fp8' else ''}RMSNorm+residual",
+                        "tokens": self.T, "hidden": H, "l2": "inputs larger than L2 (168 MB)"}
+        elif name == "silu":
+            self.x = wl.silu_inputs(device)
+            self.T = self.x.shape[0]
+            self.out = torch.empty(self.T, self.x.shape[1] // 2, dtype=self.x.dtype, device=device)
+            self.bytes = 6 * self.T * self.out.shape[1]
+            self.cfg = {"workload": "config 2 SiLU-mul", "tokens": self.T, "d": self.out.shape[1],
+                        "l2": "inputs larger than L2 (1.6 GB)"}
+        elif name == "rope":
+            self.pos, self.q, self.k, self.cache = wl.rope_inputs(device)
+            self.T = self.pos.shape[0]
+            self.bytes = self.T * (2 * 2 * (self.q.shape[1] + self.k.shape[1]) + 4 * 128 + 4)
+            self.cfg = {"workload": "config 3 rope q[T,32,128] k[T,8,128]", "tokens": self.T,
+                        "l2": "inputs larger than L2 (689 MB)"}
+        elif name == "embed":
+            self.table, self.ids = wl.embed_inputs(device)
+            self.T = self.ids.shape[0]
+            self.out = torch.empty(self.T, self.table.shape[1], dtype=self.table.dtype, device=device)
+            self.bytes = 2 * 2 * self.T * self.table.shape[1] + 4 * self.T
+            self.cfg = {"workload": "config 4 embedding gather", "tokens": self.T, "hidden": self.table.shape[1],
+                        "l2": "table 1.34 GB > L2; output 168 MB > L2"}
+        else:
+            raise ValueError(name)
+        self.tokens = self.T
+        self.global_tokens = self.T * dist.world
+        self.layers = 1
+
+    def step(self, dom_events=None):
+        st = torch.cuda.current_stream()
+        if dom_events is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+        o, n = self.o, self.name
+        if n == "norm":
+            o.fused_add_rmsnorm(self.x, self.r, self.w, self.eps, enable_pdl=True)
+        elif n == "norm_fp8":
+            o.fused_add_rmsnorm_quant(self.out, self.x, self.r, self.w, self.scale, self.eps, enable_pdl=True)
+        elif n == "silu":
+            o.silu_and_mul(self.x, out=self.out, enable_pdl=True)
+        elif n == "rope":
+            o.apply_rope_with_cos_sin_cache_inplace(self.pos, self.q, self.k, 128, self.cache, is_neox=True)
+        elif n == "embed":
+            o.embedding_out(self.out, self.ids, self.table)
+        if dom_events is not None:
+            e1.record(st)
+            dom_events.append((e0, e1))
+
+    def launches_per_step(self) -> int:
+        return 1
+
+    def step_bytes(self) -> int:
+        return self.bytes
+
+    def dominant_bytes_per_launch(self) -> int:
+        return self.bytes
+
+    def config(self) -> dict:
+        return dict(self.cfg, parallelism="token-sharded dp")
+
+
+# --------------------------------------------------------------------------------------------------
+# CPU arm: the C oracle on a token sample of the chain.
+# --------------------------------------------------------------------------------------------------
+class CpuChainSample:
+    """The oracle running the chain on `tokens` sampled tokens (all layers), inputs on the host."""
+
+    def __init__(self, tokens: int, layers: int, seed: int = 4):
+        import oracle
+        from mas_b200 import workloads as wl
+
+        s = wl.CHAIN_SHAPE
+        self.s, self.oracle, self.layers, self.tokens = s, oracle, layers, tokens
+        ids, pos = wl.chain_host_inputs(seed=seed)
+        sel = torch.linspace(0, ids.shape[0] - 1, tokens).long()
+        self.ids, self.pos = ids[sel].contiguous(), pos[sel].contiguous()
+        g = torch.Generator().manual_seed(seed)
+        # only the table rows the sample touches are materialised (the rest are never read)
+        uniq, inv = torch.unique(self.ids, return_inverse=True)
+        self.table = (torch.randn(uniq.shape[0], s.hidden_size, generator=g) * 0.02).to(torch.bfloat16)
+        self.local_ids = inv.to(torch.int64)
+        self.attn = torch.randn(tokens, s.hidden_size, generator=g).to(torch.bfloat16)
+        self.qkv = torch.randn(tokens, s.qkv_size, generator=g).to(torch.bfloat16)
+        self.gate_up = torch.randn(tokens, 2 * s.intermediate_size, generator=g).to(torch.bfloat16)
+        self.act = torch.empty(tokens, s.intermediate_size, dtype=torch.bfloat16)
+        self.w_in = (1 + 0.1 * torch.randn(layers, s.hidden_size, generator=g)).to(torch.bfloat16)
+        self.w_post = (1 + 0.1 * torch.randn(layers, s.hidden_size, generator=g)).to(torch.bfloat16)
+        from mas_b200.rope_cache import plain_cos_sin_cache
+
+        self.cache = plain_cos_sin_cache(s.head_dim, s.max_position_embeddings, s.rope_theta)
+
+    def step(self):
+        o, s = self.oracle, self.s
+        hidden, _ = o.embedding(self.local_ids, self.table)
+        residual = torch.zeros_like(hidden)
+        q = self.qkv[:, : s.q_size]
+        k = self.qkv[:, s.q_size: s.q_size + s.kv_size]
+        for l in range(self.layers):
+            o.fused_add_rmsnorm(hidden, residual, self.w_in[l], s.rms_norm_eps)
+            o.apply_rope_with_cos_sin_cache_inplace(self.pos, q, k, s.head_dim, self.cache)
+            o.fused_add_rmsnorm(self.attn, residual, self.w_post[l], s.rms_norm_eps)
+            o.silu_and_mul(self.gate_up, out=self.act)
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def calibrate_cpu_tokens(layers: int, target_s: float) -> int:
+    probe = CpuChainSample(16, layers)
+    t0 = time.perf_counter()
+    probe.step()
+    per_token = (time.perf_counter() - t0) / 16
+    return int(max(16, min(4352, target_s / max(per_token, 1e-9))))
+
+
+def time_cpu_chain(tokens: int, layers: int, reps: int) -> tuple[float, list[float]]:
+    w = CpuChainSample(tokens, layers)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        w.step()
+        times.append(time.perf_counter() - t0)
+    return tokens / statistics.median(times), times
+
+
+# --------------------------------------------------------------------------------------------------
+# Arms.
+# --------------------------------------------------------------------------------------------------
+def run_reference_arm(args, dist: Dist) -> None:
+    """The reference's CPU path on this host (C oracle port, all threads), rank 0 only."""
+    if dist.rank != 0:
+        return
+    import oracle
+
+    cores = host_cores()
+    oracle.set_num_threads(cores)
+    layers = args.layers or 88
+    if args.workload != "chain":
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm is defined for the chain workload"}))
+        return
+    per_step_budget = max(0.5, min(4.0, 150.0 / max(1, args.steps + args.warmup)))
+    tokens = calibrate_cpu_tokens(layers, per_step_budget)
+    w = CpuChainSample(tokens, layers)
+    for _ in range(args.warmup):
+        w.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        w.step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = tokens / dt
+    s = w.s
+    from mas_b200.chain import LayerChain
+
+    chain = LayerChain(s, layers=layers)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": dict(chain_config(layers, 4352, 4352), tokens_sampled_per_step=tokens),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{tokens} of 4352 tokens per step, all {layers} layers, C oracle (OpenMP)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "hbm_gbs_equivalent": chain.step_bytes(tokens) / dt / 1e9,
+    }
+    print(json.dumps(line))
+
+
+def run_gpu_arm(args, dist: Dist) -> None:
+    device = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(device)
+    if args.impl == "flashinfer":
+        ops = FlashinferOps()
+    else:
+        ops = mas_ops()
+        import mas_b200
+
+        mas_b200.prepare_device(device.index)
+    layers = args.layers or 88
+    w = ChainWorkload(device, dist, ops, layers) if args.workload == "chain" else OpWorkload(args.workload, device, dist, ops)
+
+    st = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        w.step()
+    torch.cuda.synchronize()
+
+    # ---- device-resident timed region -----------------------------------------------------------
+    dom = []
+    with Clocks(device.index) as clocks:
+        time.sleep(0.25)
+        dist.barrier()
+        torch.cuda.synchronize()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(st)
+        for _ in range(args.steps):
+            w.step(dom_events=dom if not args.no_kernel_events else None)
+        e_end.record(st)
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms = e_start.elapsed_time(e_end) / args.steps
+    ms = dist.max(ms, device)
+    dom_ms = statistics.fmean(a.elapsed_time(b) for a, b in dom) if dom else None
+    if dom_ms is not None:
+        dom_ms = dist.max(dom_ms, device)
+
+    # ---- end-to-end through the public API with host inputs/outputs --------------------------------
+    e2e = None
+    if args.workload == "chain" and not args.no_e2e:
+        for _ in range(max(1, args.warmup // 2)):
+            w.e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for _ in range(args.steps):
+            w.e2e_step()
+        b.record(st)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e2e_ms = dist.max(a.elapsed_time(b) / args.steps, device)
+        h2d, d2h = w.e2e_bytes()
+        e2e = {"value": w.global_tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "path": "public API (mas_b200 ops), pinned host ids+positions in, residual stream out"}
+
+    # ---- CPU baseline (rank 0, N = 1) ----------------------------------------------------------------
+    cpu = None
+    if args.workload == "chain" and dist.world == 1 and not args.no_cpu_baseline and args.impl != "flashinfer":
+        import oracle
+
+        cores = host_cores()
+        oracle.set_num_threads(cores)
+        tokens = calibrate_cpu_tokens(layers, 3.0)
+        value_cpu, times = time_cpu_chain(tokens, layers, reps=3)
+        cpu = {"value": value_cpu, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{tokens} of {w.tokens} tokens, all {layers} layers, C oracle, median of 3 steps "
+                         f"({sum(times):.1f} s of CPU work)"}
+
+    if dist.rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    step_s = ms / 1e3
+    value = w.global_tokens / step_s
+    gbs = w.step_bytes() / step_s / 1e9  # per GPU
+    roof = None
+    if dom_ms is not None:
+        achieved = w.dominant_bytes_per_launch() / (dom_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": w.dominant, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                "traffic": args.traffic, "bytes_per_launch": w.dominant_bytes_per_launch(),
+                "avg_launch_us": dom_ms * 1e3, "launches_timed": len(dom)}
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, random ids/positions)",
+        "config": w.config(),
+        "hbm_gbs_per_gpu": gbs, "hbm_frac_of_measured_peak": gbs / peak,
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": (w.launches_per_step() * args.steps) if args.impl == "mas" else 0,
+        "clocks": clocks.summary(),
+    }
+    if args.impl != "mas":
+        line["impl"] = args.impl
+    print(json.dumps(line))
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["mas", "reference", "flashinfer"], default="mas")
+    ap.add_argument("--workload", choices=["chain", "norm", "norm_fp8", "silu", "rope", "embed"], default="chain")
+    ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernel-events", action="store_true", help="time the region without per-launch events")
+    ap.add_argument("--traffic", type=float, default=None, help="ncu DRAM bytes per dominant launch, if known")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        # CPU only: no process group; under torchrun rank 0 runs and the other ranks exit at once.
+        run_reference_arm(args, Dist(backend="none"))
+        return
+    dist = Dist()
+    try:
+        run_gpu_arm(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,453 @@
+// mas_b200.cu -- the C ABI (include/mas_b200.h): argument checks, path choice, launch shapes.
+//
+// One translation unit holds every kernel, so the library is a single fatbin for sm_100a and needs
+// no relocatable device code. Entry points never allocate or synchronise; the only per-process
+// state is the per-device set-up of mas_prepare_device (shared-memory opt-in, SM count, the address
+// of the fault word), done once per device under a lock.
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <mutex>
+
+#include "common.cuh"
+#include "embed.cuh"
+#include "norm.cuh"
+#include "rope.cuh"
+#include "silu.cuh"
+
+namespace mas {
+
+// Library fault word: bulk-copy wait timeouts of kernels without a caller status word land here.
+__device__ int32_t g_fault_word;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr size_t kMaxSmemPerCta = 227 * 1024;
+constexpr size_t kRingBytesPerSm = 192 * 1024;  // shared memory the TMA rings may use per SM
+
+struct DeviceState {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  int sm_count = 0;
+  int32_t* fault = nullptr;
+};
+DeviceState g_dev[kMaxDevices];
+
+// Optional integer override from the environment (tuning knobs, read once per process).
+int env_int(const char* name, int fallback) {
+  const char* v = std::getenv(name);
+  if (v == nullptr || *v == '\0') return fallback;
+  return std::atoi(v);
+}
+
+template <typename K>
+cudaError_t opt_in_smem(K kernel) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kMaxSmemPerCta);
+}
+
+template <typename T, bool Q>
+cudaError_t opt_in_norm() {
+  cudaError_t e = cudaSuccess;
+  if (e == cudaSuccess) e = opt_in_smem(norm_tma_kernel<T, 1, Q>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_tma_kernel<T, 2, Q>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_tma_kernel<T, 3, Q>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_tma_kernel<T, 4, Q>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_tma_kernel<T, 5, Q>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_tma_kernel<T, 6, Q>);
+  return e;
+}
+
+cudaError_t prepare_current(DeviceState& st, int device) {
+  cudaError_t e = cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) return e;
+  if ((e = opt_in_norm<__nv_bfloat16, false>()) != cudaSuccess) return e;
+  if ((e = opt_in_norm<__nv_bfloat16, true>()) != cudaSuccess) return e;
+  if ((e = opt_in_norm<__half, false>()) != cudaSuccess) return e;
+  if ((e = opt_in_norm<__half, true>()) != cudaSuccess) return e;
+  if ((e = opt_in_smem(embed_tma_kernel<int32_t>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(embed_tma_kernel<int64_t>)) != cudaSuccess) return e;
+  void* fault = nullptr;
+  if ((e = cudaGetSymbolAddress(&fault, g_fault_word)) != cudaSuccess) return e;
+  st.fault = static_cast<int32_t*>(fault);
+  return cudaSuccess;
+}
+
+// Runs the one-time set-up of `device` with that device current, restoring the caller's device.
+int prepare(int device) {
+  if (device < 0 || device >= kMaxDevices) return MAS_ERR_INVALID_ARGUMENT;
+  DeviceState& st = g_dev[device];
+  std::call_once(st.once, [&] {
+    int prev = -1;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e == cudaSuccess && prev != device) e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = prepare_current(st, device);
+    if (prev >= 0 && prev != device) (void)cudaSetDevice(prev);
+    st.err = e;
+  });
+  return st.err == cudaSuccess ? MAS_OK : (int)st.err;
+}
+
+// Current device, prepared. Returns a status code; on success *out points at its state.
+int current_device(DeviceState** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
+    (void)cudaGetLastError();
+    return MAS_ERR_NO_DEVICE;
+  }
+  const int rc = prepare(dev);
+  if (rc != MAS_OK) return rc;
+  *out = &g_dev[dev];
+  return MAS_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, void* stream, int pdl,
+           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return e == cudaSuccess ? MAS_OK : (int)e;
+}
+
+// Resident CTAs per SM of `kernel` at this block size and dynamic shared memory, cached per
+// (device, kernel, block, smem) because the occupancy query is not free.
+struct OccKey {
+  int dev;
+  const void* fn;
+  int nt;
+  size_t smem;
+};
+std::mutex g_occ_mu;
+OccKey g_occ_key[256];
+int g_occ_val[256];
+int g_occ_n = 0;
+
+int resident_ctas(const void* fn, int nt, size_t smem) {
+  int dev = 0;
+  (void)cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(g_occ_mu);
+    for (int i = 0; i < g_occ_n; ++i)
+      if (g_occ_key[i].dev == dev && g_occ_key[i].fn == fn && g_occ_key[i].nt == nt &&
+          g_occ_key[i].smem == smem)
+        return g_occ_val[i];
+  }
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, nt, smem) != cudaSuccess) {
+    (void)cudaGetLastError();
+    blocks = 1;
+  }
+  if (blocks < 1) blocks = 1;
+  std::lock_guard<std::mutex> lk(g_occ_mu);
+  if (g_occ_n < 256) {
+    g_occ_key[g_occ_n] = OccKey{dev, fn, nt, smem};
+    g_occ_val[g_occ_n] = blocks;
+    ++g_occ_n;
+  }
+  return blocks;
+}
+
+template <typename T, bool Q>
+const void* norm_tma_fn(int vpt) {
+  switch (vpt) {
+    case 1: return (const void*)norm_tma_kernel<T, 1, Q>;
+    case 2: return (const void*)norm_tma_kernel<T, 2, Q>;
+    case 3: return (const void*)norm_tma_kernel<T, 3, Q>;
+    case 4: return (const void*)norm_tma_kernel<T, 4, Q>;
+    case 5: return (const void*)norm_tma_kernel<T, 5, Q>;
+    case 6: return (const void*)norm_tma_kernel<T, 6, Q>;
+    default: return nullptr;
+  }
+}
+
+inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ------------------------------------------------------------------------------------------
+// Fused add RMSNorm (both variants).
+// ------------------------------------------------------------------------------------------
+template <typename T, bool Q>
+int launch_norm_tma(NormArgs a, int vpt, int nt, size_t smem, int grid, void* stream, int pdl) {
+  switch (vpt) {
+    case 1: return launch(norm_tma_kernel<T, 1, Q>, dim3(grid), dim3(nt), smem, stream, pdl, a);
+    case 2: return launch(norm_tma_kernel<T, 2, Q>, dim3(grid), dim3(nt), smem, stream, pdl, a);
+    case 3: return launch(norm_tma_kernel<T, 3, Q>, dim3(grid), dim3(nt), smem, stream, pdl, a);
+    case 4: return launch(norm_tma_kernel<T, 4, Q>, dim3(grid), dim3(nt), smem, stream, pdl, a);
+    case 5: return launch(norm_tma_kernel<T, 5, Q>, dim3(grid), dim3(nt), smem, stream, pdl, a);
+    case 6: return launch(norm_tma_kernel<T, 6, Q>, dim3(grid), dim3(nt), smem, stream, pdl, a);
+    default: return MAS_ERR_UNSUPPORTED_SHAPE;
+  }
+}
+
+template <typename T, bool Q>
+int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int pdl) {
+  const int H = a.H;
+  if (fast_ok && H % 8 == 0) {
+    const int nv = H / 8;
+    const int vpt = (int)ceil_div(nv, 512);
+    const int nt = (int)ceil_div(ceil_div(nv, vpt), 32) * 32;
+    const size_t stage = 2ull * (size_t)H * sizeof(T);
+    static const int env_ctas = env_int("MAS_NORM_CTAS_PER_SM", 0);
+    static const int env_stages = env_int("MAS_NORM_STAGES", 0);
+    // CTAs per SM: as many as threads allow while each keeps at least a 2-stage ring.
+    int ctas = (int)std::min<int64_t>(2048 / nt, (int64_t)(kRingBytesPerSm / (2 * stage)));
+    if (env_ctas > 0) ctas = env_ctas;
+    if (ctas < 1) ctas = 1;
+    int stages = (int)(kRingBytesPerSm / ((size_t)ctas * stage));
+    if (env_stages > 0) stages = env_stages;
+    stages = std::max(2, std::min(8, stages));
+    const size_t smem = norm_tma_smem_bytes(H, stages, (int)sizeof(T));
+    const void* fn = norm_tma_fn<T, Q>(vpt);
+    if (fn != nullptr && smem <= kMaxSmemPerCta) {
+      ctas = std::min(ctas, resident_ctas(fn, nt, smem));  // the grid must be fully resident
+      int64_t grid = std::min<int64_t>(a.rows, (int64_t)st.sm_count * ctas);
+      a.rows_per_cta = (int32_t)ceil_div(a.rows, grid);
+      grid = ceil_div(a.rows, a.rows_per_cta);
+      a.stages = stages;
+      return launch_norm_tma<T, Q>(a, vpt, nt, smem, (int)grid, stream, pdl);
+    }
+  }
+  const int64_t grid = std::min<int64_t>(a.rows, 1 << 20);
+  return launch(norm_generic_kernel<T, Q>, dim3((unsigned)grid), dim3(256), 0, stream, pdl, a);
+}
+
+int check_act_dtype(int dtype) {
+  return (dtype == MAS_DTYPE_BF16 || dtype == MAS_DTYPE_FP16) ? MAS_OK : MAS_ERR_UNSUPPORTED_DTYPE;
+}
+
+}  // namespace
+}  // namespace mas
+
+using namespace mas;
+
+extern "C" {
+
+int mas_version(void) { return (0 << 16) | 1; }
+
+const char* mas_status_string(int code) {
+  switch (code) {
+    case MAS_OK: return "ok";
+    case MAS_ERR_INVALID_ARGUMENT: return "invalid argument (null pointer, negative size or stride shorter than a row)";
+    case MAS_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
+    case MAS_ERR_UNSUPPORTED_SHAPE: return "unsupported shape";
+    case MAS_ERR_NO_DEVICE: return "no current CUDA device";
+    default:
+      if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
+      return "unknown mas_b200 status code";
+  }
+}
+
+int mas_prepare_device(int device) { return prepare(device); }
+
+int mas_read_fault_word(int device, int32_t* value, int clear) {
+  if (value == nullptr) return MAS_ERR_INVALID_ARGUMENT;
+  int rc = prepare(device);
+  if (rc != MAS_OK) return rc;
+  int prev = -1;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e == cudaSuccess && prev != device) e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(value, g_fault_word, sizeof(int32_t));
+  if (e == cudaSuccess && clear) {
+    const int32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_fault_word, &zero, sizeof(int32_t));
+  }
+  if (prev >= 0 && prev != device) (void)cudaSetDevice(prev);
+  return e == cudaSuccess ? MAS_OK : (int)e;
+}
+
+int mas_fused_add_rmsnorm(void* input, void* residual, const void* weight, int64_t num_tokens,
+                          int64_t hidden_size, int64_t input_stride, int64_t residual_stride,
+                          float eps, int dtype, int enable_pdl, void* stream) {
+  if (num_tokens < 0 || hidden_size <= 0 || hidden_size > INT32_MAX) return MAS_ERR_INVALID_ARGUMENT;
+  if (check_act_dtype(dtype) != MAS_OK) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (num_tokens == 0) return MAS_OK;
+  if (!input || !residual || !weight) return MAS_ERR_INVALID_ARGUMENT;
+  if (input_stride < hidden_size || residual_stride < hidden_size) return MAS_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device(&st);
+  if (rc != MAS_OK) return rc;
+  NormArgs a = {};
+  a.x = input; a.r = residual; a.w = weight; a.out = nullptr; a.scale = nullptr;
+  a.rows = num_tokens; a.x_stride = input_stride; a.r_stride = residual_stride; a.out_stride = 0;
+  a.H = (int32_t)hidden_size; a.eps = eps; a.fault = st->fault;
+  const bool fast_ok = aligned(input, 16) && aligned(residual, 16) && aligned(weight, 16) &&
+                       input_stride % 8 == 0 && residual_stride % 8 == 0;
+  if (dtype == MAS_DTYPE_BF16) return run_norm<__nv_bfloat16, false>(a, *st, fast_ok, stream, enable_pdl);
+  return run_norm<__half, false>(a, *st, fast_ok, stream, enable_pdl);
+}
+
+int mas_fused_add_rmsnorm_quant(void* out, const void* input, void* residual, const void* weight,
+                                const float* scale, int64_t num_tokens, int64_t hidden_size,
+                                int64_t out_stride, int64_t input_stride, int64_t residual_stride,
+                                float eps, int dtype, int out_dtype, int enable_pdl, void* stream) {
+  if (num_tokens < 0 || hidden_size <= 0 || hidden_size > INT32_MAX) return MAS_ERR_INVALID_ARGUMENT;
+  if (check_act_dtype(dtype) != MAS_OK || out_dtype != MAS_DTYPE_FP8_E4M3) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (num_tokens == 0) return MAS_OK;
+  if (!out || !input || !residual || !weight || !scale) return MAS_ERR_INVALID_ARGUMENT;
+  if (input_stride < hidden_size || residual_stride < hidden_size || out_stride < hidden_size)
+    return MAS_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device(&st);
+  if (rc != MAS_OK) return rc;
+  NormArgs a = {};
+  a.x = const_cast<void*>(input); a.r = residual; a.w = weight;
+  a.out = static_cast<uint8_t*>(out); a.scale = scale;
+  a.rows = num_tokens; a.x_stride = input_stride; a.r_stride = residual_stride;
+  a.out_stride = out_stride; a.H = (int32_t)hidden_size; a.eps = eps; a.fault = st->fault;
+  const bool fast_ok = aligned(input, 16) && aligned(residual, 16) && aligned(weight, 16) &&
+                       aligned(out, 8) && input_stride % 8 == 0 && residual_stride % 8 == 0 &&
+                       out_stride % 8 == 0;
+  if (dtype == MAS_DTYPE_BF16) return run_norm<__nv_bfloat16, true>(a, *st, fast_ok, stream, enable_pdl);
+  return run_norm<__half, true>(a, *st, fast_ok, stream, enable_pdl);
+}
+
+int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                     int64_t out_stride, int64_t input_stride, int dtype, int enable_pdl,
+                     void* stream) {
+  if (num_tokens < 0 || d < 0 || d > (INT32_MAX / 2)) return MAS_ERR_INVALID_ARGUMENT;
+  if (check_act_dtype(dtype) != MAS_OK) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (num_tokens == 0 || d == 0) return MAS_OK;
+  if (!out || !input) return MAS_ERR_INVALID_ARGUMENT;
+  if (input_stride < 2 * d || out_stride < d) return MAS_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device(&st);
+  if (rc != MAS_OK) return rc;
+  SiluArgs a = {};
+  a.out = out; a.in = input; a.rows = num_tokens; a.in_stride = input_stride;
+  a.out_stride = out_stride; a.d = (int32_t)d;
+  const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, 65535);
+  const bool vec = d % 8 == 0 && aligned(out, 16) && aligned(input, 16) && input_stride % 8 == 0 &&
+                   out_stride % 8 == 0;
+  if (vec) {
+    constexpr int U = 4;
+    const int64_t nvec = d / 8;
+    const unsigned gx = (unsigned)ceil_div(nvec, kSiluThreads * U);
+    if (dtype == MAS_DTYPE_BF16)
+      return launch(silu_mul_vec_kernel<__nv_bfloat16, U>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+    return launch(silu_mul_vec_kernel<__half, U>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+  }
+  const unsigned gx = (unsigned)std::min<int64_t>(ceil_div(d, kSiluThreads), 1 << 16);
+  if (dtype == MAS_DTYPE_BF16)
+    return launch(silu_mul_generic_kernel<__nv_bfloat16>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+  return launch(silu_mul_generic_kernel<__half>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+}
+
+int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, void* query,
+                                   void* key, const float* cos_sin_cache, int64_t num_tokens,
+                                   int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                                   int64_t rotary_dim, int64_t max_positions,
+                                   int64_t q_stride_token, int64_t q_stride_head,
+                                   int64_t k_stride_token, int64_t k_stride_head, int is_neox,
+                                   int dtype, int32_t* status, int enable_pdl, void* stream) {
+  if (num_tokens < 0 || num_q_heads < 0 || num_kv_heads < 0 || head_size <= 0 ||
+      max_positions < 0 || num_q_heads + num_kv_heads > INT32_MAX)
+    return MAS_ERR_INVALID_ARGUMENT;
+  if (check_act_dtype(dtype) != MAS_OK) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (positions_dtype != MAS_DTYPE_INT32 && positions_dtype != MAS_DTYPE_INT64)
+    return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (rotary_dim <= 0 || rotary_dim % 2 != 0 || rotary_dim > head_size) return MAS_ERR_UNSUPPORTED_SHAPE;
+  const int64_t NH = num_q_heads + num_kv_heads;
+  if (num_tokens == 0 || NH == 0) return MAS_OK;
+  if (!positions || !cos_sin_cache) return MAS_ERR_INVALID_ARGUMENT;
+  if ((num_q_heads > 0 && !query) || (num_kv_heads > 0 && !key)) return MAS_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device(&st);
+  if (rc != MAS_OK) return rc;
+  RopeArgs a = {};
+  a.pos = positions; a.q = query; a.k = key; a.cache = cos_sin_cache;
+  a.T = num_tokens; a.P = max_positions;
+  a.qsn = q_stride_token; a.qsh = q_stride_head; a.ksn = k_stride_token; a.ksh = k_stride_head;
+  a.Hq = (int32_t)num_q_heads; a.Hkv = (int32_t)num_kv_heads; a.rd = (int32_t)rotary_dim;
+  a.status = status;
+  const bool q_al = num_q_heads == 0 || (aligned(query, 16) && q_stride_token % 8 == 0 && q_stride_head % 8 == 0);
+  const bool k_al = num_kv_heads == 0 || (aligned(key, 16) && k_stride_token % 8 == 0 && k_stride_head % 8 == 0);
+  const bool vec = rotary_dim % 16 == 0 && rotary_dim / 16 <= 32 && q_al && k_al &&
+                   aligned(cos_sin_cache, 16) && num_tokens * NH < (int64_t)INT32_MAX;
+  const bool i64 = positions_dtype == MAS_DTYPE_INT64;
+  const bool bf = dtype == MAS_DTYPE_BF16;
+  const bool neox = is_neox != 0;
+  const dim3 blk(kRopeThreads);
+#define MAS_ROPE_LAUNCH(KERNEL, GRID)                                                              \
+  do {                                                                                             \
+    if (bf) {                                                                                      \
+      if (i64) return neox ? launch(KERNEL<__nv_bfloat16, int64_t, true>, GRID, blk, 0, stream, enable_pdl, a) \
+                           : launch(KERNEL<__nv_bfloat16, int64_t, false>, GRID, blk, 0, stream, enable_pdl, a); \
+      return neox ? launch(KERNEL<__nv_bfloat16, int32_t, true>, GRID, blk, 0, stream, enable_pdl, a)  \
+                  : launch(KERNEL<__nv_bfloat16, int32_t, false>, GRID, blk, 0, stream, enable_pdl, a); \
+    }                                                                                              \
+    if (i64) return neox ? launch(KERNEL<__half, int64_t, true>, GRID, blk, 0, stream, enable_pdl, a) \
+                         : launch(KERNEL<__half, int64_t, false>, GRID, blk, 0, stream, enable_pdl, a); \
+    return neox ? launch(KERNEL<__half, int32_t, true>, GRID, blk, 0, stream, enable_pdl, a)        \
+                : launch(KERNEL<__half, int32_t, false>, GRID, blk, 0, stream, enable_pdl, a);      \
+  } while (0)
+  if (vec) {
+    a.tpu = (int32_t)(rotary_dim / 16);
+    const int64_t upb = kRopeThreads / a.tpu;
+    const dim3 grid((unsigned)std::min<int64_t>(ceil_div(num_tokens * NH, upb), INT32_MAX));
+    MAS_ROPE_LAUNCH(rope_vec_kernel, grid);
+  }
+  const int64_t pairs = num_tokens * NH * (rotary_dim / 2);
+  const dim3 grid((unsigned)std::min<int64_t>(ceil_div(pairs, kRopeThreads), 1 << 22));
+  MAS_ROPE_LAUNCH(rope_generic_kernel, grid);
+#undef MAS_ROPE_LAUNCH
+}
+
+int mas_embedding_gather(void* out, const void* table, const void* ids, int ids_dtype,
+                         int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
+                         int64_t out_stride, int64_t table_stride, int elem_size,
+                         int32_t* status, int enable_pdl, void* stream) {
+  if (num_tokens < 0 || hidden_size <= 0 || vocab_size < 0) return MAS_ERR_INVALID_ARGUMENT;
+  if (elem_size != 1 && elem_size != 2 && elem_size != 4 && elem_size != 8) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (ids_dtype != MAS_DTYPE_INT32 && ids_dtype != MAS_DTYPE_INT64) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (num_tokens == 0) return MAS_OK;
+  if (!out || !table || !ids) return MAS_ERR_INVALID_ARGUMENT;
+  if (out_stride < hidden_size || table_stride < hidden_size) return MAS_ERR_INVALID_ARGUMENT;
+  const int64_t row_bytes = hidden_size * elem_size;
+  if (row_bytes > INT32_MAX) return MAS_ERR_UNSUPPORTED_SHAPE;
+  DeviceState* st = nullptr;
+  int rc = current_device(&st);
+  if (rc != MAS_OK) return rc;
+  EmbedArgs a = {};
+  a.out = out; a.table = table; a.ids = ids; a.T = num_tokens; a.V = vocab_size;
+  a.out_stride_b = out_stride * elem_size; a.table_stride_b = table_stride * elem_size;
+  a.row_bytes = (uint32_t)row_bytes; a.status = status; a.fault = st->fault;
+  const bool i64 = ids_dtype == MAS_DTYPE_INT64;
+  const bool tma = row_bytes % 16 == 0 && row_bytes <= 64 * 1024 && aligned(out, 16) &&
+                   aligned(table, 16) && a.out_stride_b % 16 == 0 && a.table_stride_b % 16 == 0;
+  if (tma) {
+    static const int env_stages = env_int("MAS_EMBED_STAGES", 0);
+    int stages = env_stages > 0 ? env_stages : (int)std::max<int64_t>(2, std::min<int64_t>(8, (48 * 1024) / row_bytes));
+    stages = std::max(2, std::min(16, stages));
+    const size_t ring = (size_t)stages * (size_t)row_bytes + 8 * (size_t)kEmbedMaxRowsPerCta;
+    const int ctas = (int)std::max<size_t>(1, std::min<size_t>(16, kRingBytesPerSm / ring));
+    int64_t grid = std::max<int64_t>((int64_t)st->sm_count * ctas, ceil_div(num_tokens, kEmbedMaxRowsPerCta));
+    grid = std::min<int64_t>(grid, num_tokens);
+    a.rows_per_cta = (int32_t)ceil_div(num_tokens, grid);
+    grid = ceil_div(num_tokens, a.rows_per_cta);
+    a.stages = stages;
+    const size_t smem = embed_tma_smem_bytes(a.row_bytes, stages, a.rows_per_cta);
+    if (smem <= kMaxSmemPerCta && grid <= INT32_MAX) {
+      if (i64) return launch(embed_tma_kernel<int64_t>, dim3((unsigned)grid), dim3(32), smem, stream, enable_pdl, a);
+      return launch(embed_tma_kernel<int32_t>, dim3((unsigned)grid), dim3(32), smem, stream, enable_pdl, a);
+    }
+  }
+  int unit = 16;
+  while (unit > 1 && (row_bytes % unit != 0 || !aligned(out, unit) || !aligned(table, unit) ||
+                      a.out_stride_b % unit != 0 || a.table_stride_b % unit != 0))
+    unit >>= 1;
+  const dim3 grid((unsigned)std::min<int64_t>(ceil_div(num_tokens, 8), 1 << 20));
+  if (i64) return launch(embed_generic_kernel<int64_t>, grid, dim3(256), 0, stream, enable_pdl, a, unit);
+  return launch(embed_generic_kernel<int32_t>, grid, dim3(256), 0, stream, enable_pdl, a, unit);
+}
+
+}  // extern "C"

@@ -1,0 +1,391 @@
+"""Drop-in per-token layer ops for mini-agent-serve's Devstral 2 model, on the B200 CUDA kernels.
+
+The public functions keep the names, signatures, argument meaning and error behaviour of the
+flashinfer 0.6.11.post2 functions that miniagentserve/models/devstral2/devstral2.py imports
+(devstral2.py:18-23), so the module forwards call them unchanged:
+
+    fused_add_rmsnorm          FI/norm/__init__.py:236-274         devstral2.py:305-307
+    fused_add_rmsnorm_quant    FI/norm/__init__.py:288-344         devstral2.py:241-252
+    silu_and_mul               FI/activation.py:77-118             devstral2.py:223-224
+    apply_rope_with_cos_sin_cache_inplace  FI/rope.py:1223-1272    devstral2.py:163-166
+
+plus the token-embedding gather behind nn.Embedding (devstral2.py:260, :282), as `embedding` and the
+`Embedding` module (embedding.py).
+
+Each function is a thin Python check layer over a `torch.library` custom op in the `mas_b200`
+namespace (opaque to torch.compile through its fake kernel, mirroring flashinfer's
+register_custom_op/register_fake_op, FI/activation.py:48-58), whose CUDA implementation calls the
+C ABI of libmas_b200.so (include/mas_b200.h) on the current stream. There is no CPU
+implementation: the ops are registered for CUDA only, and the library must be present.
+"""
+from __future__ import annotations
+
+import warnings
+from typing import Optional, Union
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "fused_add_rmsnorm",
+    "fused_add_rmsnorm_quant",
+    "silu_and_mul",
+    "apply_rope_with_cos_sin_cache_inplace",
+    "embedding",
+    "embedding_out",
+    "status_word",
+    "read_status",
+]
+
+FP8 = torch.float8_e4m3fn
+
+_ACT_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_FP16}
+_ID_DTYPES = {torch.int32: _lib.DTYPE_INT32, torch.int64: _lib.DTYPE_INT64}
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _act_code(t: torch.Tensor) -> int:
+    try:
+        return _ACT_DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; expected bfloat16 or float16") from None
+
+
+def _rows(t: torch.Tensor, name: str) -> torch.Tensor:
+    """`t` as a 2-D [tokens, hidden] view (hidden contiguous), without copying."""
+    if t.dim() == 0:
+        raise ValueError(f"{name} must have at least one dimension")
+    if t.stride(-1) != 1 and t.shape[-1] > 1:
+        raise ValueError(f"{name} must be contiguous in its last dimension")
+    if t.dim() == 1:
+        return t.view(1, -1)
+    try:
+        return t.view(-1, t.shape[-1])
+    except RuntimeError:
+        raise ValueError(f"{name}'s leading dimensions must be collapsible into one") from None
+
+
+class _DeviceGuard:
+    """Makes `t`'s device current for the C ABI (which launches on the current device)."""
+
+    __slots__ = ("dev", "prev")
+
+    def __init__(self, t: torch.Tensor):
+        self.dev = t.device.index
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if self.dev is not None and cur != self.dev:
+            self.prev = cur
+            torch.cuda.set_device(self.dev)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+# ------------------------------------------------------------------------------------------------
+# Device status word (out-of-range ids / positions), one int32 per device.
+# ------------------------------------------------------------------------------------------------
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: Union[int, torch.device, None] = None) -> Optional[torch.Tensor]:
+    """The int32 status word the gather and rope kernels OR their MAS_STATUS_* bits into.
+
+    Created (zeroed) on first use outside stream capture; while a capture is in progress and the
+    word does not exist yet, None is returned and the kernels report nothing.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _status.get(idx)
+    if w is None:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = w
+    return w
+
+
+def read_status(device: Union[int, torch.device, None] = None, clear: bool = True) -> int:
+    """Reads (host sync) and optionally clears the status word of `device`."""
+    w = status_word(device)
+    if w is None:
+        return 0
+    v = int(w.item())
+    if clear:
+        w.zero_()
+    return v
+
+
+def _status_ptr(t: torch.Tensor) -> Optional[int]:
+    w = status_word(t.device)
+    return None if w is None else w.data_ptr()
+
+
+# ------------------------------------------------------------------------------------------------
+# Fused add RMSNorm.
+# ------------------------------------------------------------------------------------------------
+@torch.library.custom_op("mas_b200::fused_add_rmsnorm", mutates_args=("input", "residual"), device_types="cuda")
+def _fused_add_rmsnorm_op(input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                          enable_pdl: bool) -> None:
+    x, r = _rows(input, "input"), _rows(residual, "residual")
+    with _DeviceGuard(x):
+        rc = _lib.lib.mas_fused_add_rmsnorm(
+            x.data_ptr(), r.data_ptr(), weight.data_ptr(), x.shape[0], x.shape[1], x.stride(0), r.stride(0),
+            float(eps), _act_code(x), int(enable_pdl), _stream(x))
+    _lib.check("mas_fused_add_rmsnorm", rc)
+
+
+@_fused_add_rmsnorm_op.register_fake
+def _(input, residual, weight, eps, enable_pdl) -> None:
+    return None
+
+
+def _check_norm(input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor) -> None:
+    if input.shape != residual.shape:
+        raise ValueError(f"input {tuple(input.shape)} and residual {tuple(residual.shape)} differ")
+    if input.dtype != residual.dtype or weight.dtype != input.dtype:
+        raise ValueError("input, residual and weight must share one dtype")
+    if weight.dim() != 1 or weight.shape[0] != input.shape[-1] or not weight.is_contiguous():
+        raise ValueError(f"weight must be a contiguous ({input.shape[-1]},) tensor")
+    _act_code(input)
+
+
+def fused_add_rmsnorm(input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+                      enable_pdl: Optional[bool] = None) -> None:
+    r"""Fused add root mean square normalization, in place.
+
+    ``residual[i] += input[i]`` then ``input[i] = (residual[i] / RMS(residual)) * weight[i]``, with the
+    sum kept in fp32 and the norm taken over the unrounded sum (as flashinfer does).
+    Same signature and meaning as flashinfer.norm.fused_add_rmsnorm (FI/norm/__init__.py:236-274).
+    """
+    _check_norm(input, residual, weight)
+    pdl = True if enable_pdl is None else bool(enable_pdl)
+    torch.ops.mas_b200.fused_add_rmsnorm(input, residual, weight, float(eps), pdl)
+
+
+def _normalize_scale(scale: Union[float, torch.Tensor], ref: torch.Tensor) -> torch.Tensor:
+    """Scale as a (1,) fp32 tensor on `ref`'s device (FI/norm/__init__.py:84-108)."""
+    if not isinstance(scale, torch.Tensor):
+        warnings.warn("Passing scale as a float is deprecated; pass a torch.Tensor of shape (1,)",
+                      FutureWarning, stacklevel=3)
+        scale = torch.tensor([scale], dtype=torch.float32, device=ref.device)
+    if scale.device != ref.device:
+        scale = scale.to(ref.device)
+    if scale.dtype != torch.float32:
+        scale = scale.to(torch.float32)
+    if scale.ndim == 0:
+        scale = scale.view(1)
+    elif not (scale.ndim == 1 and scale.numel() == 1):
+        raise ValueError(f"scale must be a scalar tensor or shape (1,), got shape {tuple(scale.shape)}")
+    return scale.contiguous()
+
+
+@torch.library.custom_op("mas_b200::fused_add_rmsnorm_quant", mutates_args=("out", "residual"), device_types="cuda")
+def _fused_add_rmsnorm_quant_op(out: torch.Tensor, input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                                scale: torch.Tensor, eps: float, enable_pdl: bool) -> None:
+    o, x, r = _rows(out, "out"), _rows(input, "input"), _rows(residual, "residual")
+    with _DeviceGuard(x):
+        rc = _lib.lib.mas_fused_add_rmsnorm_quant(
+            o.data_ptr(), x.data_ptr(), r.data_ptr(), weight.data_ptr(), scale.data_ptr(), x.shape[0], x.shape[1],
+            o.stride(0), x.stride(0), r.stride(0), float(eps), _act_code(x), _lib.DTYPE_FP8_E4M3, int(enable_pdl),
+            _stream(x))
+    _lib.check("mas_fused_add_rmsnorm_quant", rc)
+
+
+@_fused_add_rmsnorm_quant_op.register_fake
+def _(out, input, residual, weight, scale, eps, enable_pdl) -> None:
+    return None
+
+
+def fused_add_rmsnorm_quant(out: torch.Tensor, input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                            scale: Union[float, torch.Tensor], eps: float = 1e-6,
+                            enable_pdl: Optional[bool] = None) -> None:
+    r"""Fused add root mean square normalization + fp8 (e4m3) quantisation.
+
+    ``residual[i] += input[i]`` then ``out[i] = fp8(clamp(residual[i] / RMS(residual) * weight[i] / scale,
+    -448, 448))``; `input` is left unchanged. Same signature and meaning as
+    flashinfer.norm.fused_add_rmsnorm_quant (FI/norm/__init__.py:288-344).
+    """
+    _check_norm(input, residual, weight)
+    if out.dtype != FP8:
+        raise ValueError(f"out must be {FP8}, got {out.dtype}")
+    if out.shape != input.shape:
+        raise ValueError(f"out {tuple(out.shape)} and input {tuple(input.shape)} differ")
+    scale = _normalize_scale(scale, input)
+    pdl = True if enable_pdl is None else bool(enable_pdl)
+    torch.ops.mas_b200.fused_add_rmsnorm_quant(out, input, residual, weight, scale, float(eps), pdl)
+
+
+# ------------------------------------------------------------------------------------------------
+# SiLU and mul.
+# ------------------------------------------------------------------------------------------------
+@torch.library.custom_op("mas_b200::silu_and_mul", mutates_args=("out",), device_types="cuda")
+def _silu_and_mul_op(out: torch.Tensor, input: torch.Tensor, enable_pdl: bool) -> None:
+    o, x = _rows(out, "out"), _rows(input, "input")
+    with _DeviceGuard(x):
+        rc = _lib.lib.mas_silu_and_mul(o.data_ptr(), x.data_ptr(), x.shape[0], o.shape[1], o.stride(0), x.stride(0),
+                                       _act_code(x), int(enable_pdl), _stream(x))
+    _lib.check("mas_silu_and_mul", rc)
+
+
+@_silu_and_mul_op.register_fake
+def _(out, input, enable_pdl) -> None:
+    return None
+
+
+def _check_shape(input: torch.Tensor, output: torch.Tensor) -> None:
+    """Shape agreement of input and out (FI/activation.py:65-74)."""
+    assert input.ndim == output.ndim, f"{input.ndim} != {output.ndim}"
+    assert input.shape[:-1] == output.shape[:-1], f"{input.shape[:-1]} != {output.shape[:-1]}"
+    assert input.shape[-1] == 2 * output.shape[-1], f"{input.shape[-1]} != {2 * output.shape[-1]}"
+
+
+def silu_and_mul(input: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 enable_pdl: Optional[bool] = None) -> torch.Tensor:
+    r"""Fused SiLU and mul: ``silu(input[..., :d]) * input[..., d:]``.
+
+    Same signature, checks and allocation behaviour as flashinfer.activation.silu_and_mul
+    (FI/activation.py:77-118): the last dimension must span a multiple of 16 bytes, and `out` is
+    allocated with torch.empty when not given.
+    """
+    if input.shape[-1] * input.dtype.itemsize % 16 != 0:
+        raise ValueError("The pointers must be multiple of 16 bytes.")
+    if out is not None:
+        _check_shape(input, out)
+        if out.dtype != input.dtype:
+            raise ValueError("out must have the dtype of input")
+    else:
+        out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), device=input.device, dtype=input.dtype)
+    _act_code(input)
+    pdl = True if enable_pdl is None else bool(enable_pdl)
+    torch.ops.mas_b200.silu_and_mul(out, input, pdl)
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+# Rotary embedding from the fp32 cos|sin cache.
+# ------------------------------------------------------------------------------------------------
+@torch.library.custom_op("mas_b200::apply_rope_pos_ids_cos_sin_cache", mutates_args=("q", "k"),
+                         device_types="cuda")
+def _rope_op(q: torch.Tensor, k: torch.Tensor, cos_sin_cache: torch.Tensor, pos_ids: torch.Tensor,
+             interleave: bool, enable_pdl: bool) -> None:
+    with _DeviceGuard(q):
+        status = _status_ptr(q)
+        rc = _lib.lib.mas_rope_cos_sin_cache_inplace(
+            pos_ids.data_ptr(), _ID_DTYPES[pos_ids.dtype], q.data_ptr(), k.data_ptr(), cos_sin_cache.data_ptr(),
+            q.shape[0], q.shape[1], k.shape[1], q.shape[2], cos_sin_cache.shape[1], cos_sin_cache.shape[0],
+            q.stride(0), q.stride(1), k.stride(0), k.stride(1), int(not interleave), _act_code(q), status,
+            int(enable_pdl), _stream(q))
+    _lib.check("mas_rope_cos_sin_cache_inplace", rc)
+
+
+@_rope_op.register_fake
+def _(q, k, cos_sin_cache, pos_ids, interleave, enable_pdl) -> None:
+    return None
+
+
+def apply_rope_with_cos_sin_cache_inplace(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
+                                          head_size: int, cos_sin_cache: torch.Tensor, is_neox: bool = True,
+                                          enable_pdl: Optional[bool] = None) -> None:
+    r"""Applies rotary embedding to `query` and `key` in place, with cos/sin from `cos_sin_cache`.
+
+    Same signature and meaning as flashinfer.rope.apply_rope_with_cos_sin_cache_inplace
+    (FI/rope.py:1223-1272): `query` is ``(nnz, num_q_heads * head_size)`` and `key`
+    ``(nnz, num_k_heads * head_size)`` (views of one fused qkv row are fine); `cos_sin_cache` is fp32
+    ``(max_seq_len, rotary_dim)``, cos in the first half, sin in the second; ``is_neox`` selects the
+    half-rotation (True) or the interleaved pairs (False). A ValueError is raised for a non-fp32
+    cache. `enable_pdl` (an addition; the kernels are PDL-safe) defaults to True.
+    """
+    if cos_sin_cache.dtype != torch.float32:
+        raise ValueError("cos_sin_cache should be float32")
+    if cos_sin_cache.dim() != 2 or not cos_sin_cache.is_contiguous():
+        raise ValueError("cos_sin_cache must be a contiguous (max_seq_len, rotary_dim) tensor")
+    if positions.dtype not in _ID_DTYPES:
+        raise ValueError(f"positions must be int32 or int64, got {positions.dtype}")
+    if query.dtype != key.dtype:
+        raise ValueError("query and key must share one dtype")
+    rotary_dim = cos_sin_cache.shape[1]
+    if rotary_dim % 2 != 0 or rotary_dim > head_size:
+        raise ValueError(f"rotary_dim {rotary_dim} must be even and <= head_size {head_size}")
+    if query.shape[0] != positions.shape[0] or key.shape[0] != positions.shape[0]:
+        raise ValueError("positions, query and key must have the same number of tokens")
+    if positions.shape[0] == 0:
+        return
+    q = query.view(query.shape[0], -1, head_size)
+    k = key.view(key.shape[0], -1, head_size)
+    pdl = True if enable_pdl is None else bool(enable_pdl)
+    torch.ops.mas_b200.apply_rope_pos_ids_cos_sin_cache(q, k, cos_sin_cache, positions, not is_neox, pdl)
+
+
+# ------------------------------------------------------------------------------------------------
+# Token-embedding gather.
+# ------------------------------------------------------------------------------------------------
+def _gather(out: torch.Tensor, ids: torch.Tensor, weight: torch.Tensor, enable_pdl: bool) -> None:
+    o = out.view(-1, weight.shape[1])
+    i = ids.reshape(-1)
+    with _DeviceGuard(weight):
+        rc = _lib.lib.mas_embedding_gather(
+            o.data_ptr(), weight.data_ptr(), i.data_ptr(), _ID_DTYPES[i.dtype], i.shape[0], weight.shape[1],
+            weight.shape[0], o.stride(0), weight.stride(0), weight.element_size(), _status_ptr(weight),
+            int(enable_pdl), _stream(weight))
+    _lib.check("mas_embedding_gather", rc)
+
+
+@torch.library.custom_op("mas_b200::embedding", mutates_args=(), device_types="cuda")
+def _embedding_op(input_ids: torch.Tensor, weight: torch.Tensor, enable_pdl: bool) -> torch.Tensor:
+    out = torch.empty(tuple(input_ids.shape) + (weight.shape[1],), dtype=weight.dtype, device=weight.device)
+    _gather(out, input_ids, weight, enable_pdl)
+    return out
+
+
+@_embedding_op.register_fake
+def _(input_ids, weight, enable_pdl):
+    return weight.new_empty(tuple(input_ids.shape) + (weight.shape[1],))
+
+
+@torch.library.custom_op("mas_b200::embedding_out", mutates_args=("out",), device_types="cuda")
+def _embedding_out_op(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tensor, enable_pdl: bool) -> None:
+    _gather(out, input_ids, weight, enable_pdl)
+
+
+@_embedding_out_op.register_fake
+def _(out, input_ids, weight, enable_pdl) -> None:
+    return None
+
+
+def _check_embedding(input_ids: torch.Tensor, weight: torch.Tensor) -> None:
+    if input_ids.dtype not in _ID_DTYPES:
+        raise ValueError(f"input_ids must be int32 or int64, got {input_ids.dtype}")
+    if weight.dim() != 2 or weight.stride(1) != 1:
+        raise ValueError("weight must be a (num_embeddings, embedding_dim) tensor, contiguous in its last dimension")
+
+
+def embedding(input_ids: torch.Tensor, weight: torch.Tensor, enable_pdl: Optional[bool] = None) -> torch.Tensor:
+    """``weight[input_ids]``: the row gather nn.Embedding performs (devstral2.py:260, :282), bit-exact.
+
+    An id outside ``[0, num_embeddings)`` yields a zero row and sets MAS_STATUS_EMBED_ID_OUT_OF_RANGE
+    in the device status word (`read_status`), where aten would raise a device-side assert.
+    """
+    _check_embedding(input_ids, weight)
+    pdl = True if enable_pdl is None else bool(enable_pdl)
+    return torch.ops.mas_b200.embedding(input_ids, weight, pdl)
+
+
+def embedding_out(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tensor,
+                  enable_pdl: Optional[bool] = None) -> torch.Tensor:
+    """`embedding` into a caller-owned ``(*input_ids.shape, embedding_dim)`` tensor."""
+    _check_embedding(input_ids, weight)
+    if out.shape != tuple(input_ids.shape) + (weight.shape[1],) or out.dtype != weight.dtype:
+        raise ValueError("out must be (*input_ids.shape, embedding_dim) with weight's dtype")
+    if not out.is_contiguous():
+        raise ValueError("out must be contiguous")
+    pdl = True if enable_pdl is None else bool(enable_pdl)
+    torch.ops.mas_b200.embedding_out(out, input_ids, weight, pdl)
+    return out

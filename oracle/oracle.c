@@ -1,0 +1,253 @@
+/*
+ * oracle.c -- CPU restatement of the per-token layer ops, for TESTS ONLY.
+ *
+ * This file is test infrastructure: the parity tests, __graft_entry__.smoke() and the CPU-baseline
+ * legs of bench.py call it as the checker. The product path (mini-agent-serve_b200/) never links,
+ * loads or calls it.
+ *
+ * What it restates. The reference (mini-agent-serve) computes these ops through flashinfer-python
+ * 0.6.11.post2 (not vendored in the reference; the reference pins no version) and through aten for
+ * the embedding. Each function below follows the flashinfer source it cites (paths prefixed FI/ are
+ * relative to the installed flashinfer package):
+ *   - every op does its arithmetic in fp32 and rounds once to the output type (RNE);
+ *   - transcendental and reduction steps are evaluated more accurately here (double sum of squares,
+ *     double exp and rsqrt) than on the GPU (fp32 tree sums, __expf, rsqrt.approx); the parity bar
+ *     (<= 1 bf16 ulp, or 1 e4m3 step) absorbs the difference.
+ * Compiled with -ffp-contract=off so no multiply-add is fused behind the C source's back.
+ *
+ * Every entry point mirrors the argument order of the matching C-ABI function in
+ * include/mas_b200.h (prefix orc_ instead of mas_), minus the stream and PDL flag.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORC_BF16 0
+#define ORC_FP16 1
+#define ORC_INT32 4
+#define ORC_INT64 5
+
+/* ---------------------------------------------------------------------------------------------
+ * Number formats.
+ * --------------------------------------------------------------------------------------------- */
+static inline float u32_as_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t f32_as_u32(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+/* bfloat16 is the upper half of an IEEE binary32. */
+static inline float bf16_to_f32(uint16_t h) { return u32_as_f32((uint32_t)h << 16); }
+
+/* binary32 -> bfloat16, round to nearest even; NaN stays a (quiet) NaN. */
+static inline uint16_t f32_to_bf16(float f) {
+  uint32_t u = f32_as_u32(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x0040u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+/* binary16 <-> binary32 through the compiler's _Float16 (IEEE conversions, RNE). */
+static inline float f16_to_f32(uint16_t h) { _Float16 v; memcpy(&v, &h, 2); return (float)v; }
+static inline uint16_t f32_to_f16(float f) { _Float16 v = (_Float16)f; uint16_t h; memcpy(&h, &v, 2); return h; }
+
+static inline float ld_act(const uint16_t* p, int dtype) { return dtype == ORC_BF16 ? bf16_to_f32(*p) : f16_to_f32(*p); }
+static inline uint16_t to_act(float f, int dtype) { return dtype == ORC_BF16 ? f32_to_bf16(f) : f32_to_f16(f); }
+
+/* binary32 -> float8 e4m3fn (bias 7, no infinities, max finite 448 = 0x7e, NaN = 0x7f), round to
+ * nearest even, saturating: |f| >= 448 (and +-inf) gives +-448, NaN gives NaN. This is the format's
+ * definition worked through directly: subnormals step by 2^-9, a normal with unbiased exponent E
+ * steps by 2^(E-3). */
+uint8_t orc_f32_to_e4m3(float f) {
+  if (isnan(f)) return 0x7f;
+  const uint8_t sign = signbit(f) ? 0x80 : 0x00;
+  const float a = fabsf(f);
+  if (a >= 448.0f) return sign | 0x7e;
+  if (a < 0.015625f) {                                /* below 2^-6: subnormal (or zero) */
+    const float q = rintf(a * 512.0f);                /* exact scaling, then RNE to the 2^-9 grid */
+    return sign | (uint8_t)q;                         /* q == 8 is the smallest normal, code 0x08 */
+  }
+  int e;
+  (void)frexpf(a, &e);                                /* a = m * 2^e, m in [0.5, 1) */
+  int E = e - 1;                                      /* a in [2^E, 2^(E+1)) */
+  float q = rintf(ldexpf(a, 3 - E));                  /* significand in eighths: [8, 16] */
+  if (q >= 16.0f) { q = 8.0f; E += 1; }
+  const int code = ((E + 7) << 3) | ((int)q - 8);
+  return sign | (uint8_t)(code > 0x7e ? 0x7e : code);
+}
+
+float orc_e4m3_to_f32(uint8_t b) {
+  const float s = (b & 0x80) ? -1.0f : 1.0f;
+  const int e = (b >> 3) & 0xf, m = b & 0x7;
+  if (e == 0xf && m == 0x7) return NAN;
+  if (e == 0) return s * ldexpf((float)m, -9);
+  return s * ldexpf((float)(8 + m), e - 10);
+}
+
+uint16_t orc_f32_to_bf16(float f) { return f32_to_bf16(f); }
+float orc_bf16_to_f32(uint16_t h) { return bf16_to_f32(h); }
+uint16_t orc_f32_to_f16(float f) { return f32_to_f16(f); }
+
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
+int orc_get_num_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/* ---------------------------------------------------------------------------------------------
+ * Fused add RMSNorm. FI/norm/kernels/fused_add_rmsnorm.py:380-406 (bf16 out) and :700-728 (fp8
+ * out); FI/data/include/flashinfer/norm.cuh:405-479 and :537-600:
+ *   h = f32(x) + f32(r);  r <- round(h);  rstd = 1/sqrt(sum(h^2)/H + eps);
+ *   y = h * rstd * w   (left to right, fp32);  x <- round(y)   or   out <- e4m3(y * (1/scale)).
+ * The norm uses the unrounded fp32 h, not round(h).
+ * --------------------------------------------------------------------------------------------- */
+static void norm_rows(void* out, void* input, void* residual, const void* weight, const float* scale,
+                      int64_t T, int64_t H, int64_t out_stride, int64_t in_stride,
+                      int64_t res_stride, float eps, int dtype, int quant) {
+  const uint16_t* w = (const uint16_t*)weight;
+  const float inv_scale = quant ? 1.0f / scale[0] : 1.0f;
+#pragma omp parallel
+  {
+    float* h = (float*)malloc((size_t)H * sizeof(float));
+#pragma omp for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+      uint16_t* x = (uint16_t*)input + t * in_stride;
+      uint16_t* r = (uint16_t*)residual + t * res_stride;
+      double ss = 0.0;
+      for (int64_t j = 0; j < H; ++j) {
+        const float v = ld_act(&x[j], dtype) + ld_act(&r[j], dtype);
+        h[j] = v;
+        ss += (double)v * (double)v;
+      }
+      const float rstd = (float)(1.0 / sqrt(ss / (double)H + (double)eps));
+      for (int64_t j = 0; j < H; ++j) {
+        r[j] = to_act(h[j], dtype);
+        const float y = h[j] * rstd * ld_act(&w[j], dtype);
+        if (quant)
+          ((uint8_t*)out)[t * out_stride + j] = orc_f32_to_e4m3(y * inv_scale);
+        else
+          x[j] = to_act(y, dtype);
+      }
+    }
+    free(h);
+  }
+}
+
+int orc_fused_add_rmsnorm(void* input, void* residual, const void* weight, int64_t num_tokens,
+                          int64_t hidden_size, int64_t input_stride, int64_t residual_stride,
+                          float eps, int dtype) {
+  if (num_tokens < 0 || hidden_size <= 0 || (dtype != ORC_BF16 && dtype != ORC_FP16)) return -1;
+  norm_rows(NULL, input, residual, weight, NULL, num_tokens, hidden_size, 0, input_stride,
+            residual_stride, eps, dtype, 0);
+  return 0;
+}
+
+int orc_fused_add_rmsnorm_quant(void* out, const void* input, void* residual, const void* weight,
+                                const float* scale, int64_t num_tokens, int64_t hidden_size,
+                                int64_t out_stride, int64_t input_stride, int64_t residual_stride,
+                                float eps, int dtype) {
+  if (num_tokens < 0 || hidden_size <= 0 || (dtype != ORC_BF16 && dtype != ORC_FP16)) return -1;
+  norm_rows(out, (void*)input, residual, weight, scale, num_tokens, hidden_size, out_stride,
+            input_stride, residual_stride, eps, dtype, 1);
+  return 0;
+}
+
+/* ---------------------------------------------------------------------------------------------
+ * SiLU and mul. FI/data/include/flashinfer/activation.cuh:43-49 with FI/jit/activation.py:77-80:
+ *   out = round(silu(g) * u),  silu(g) = g / (1 + exp(-g)),  all fp32.
+ * exp is evaluated in double and rounded to fp32 (so it overflows to +inf exactly where the fp32
+ * exponential does, g < about -88.72, giving silu = -0 there like the GPU).
+ * --------------------------------------------------------------------------------------------- */
+int orc_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                     int64_t out_stride, int64_t input_stride, int dtype) {
+  if (num_tokens < 0 || d < 0 || (dtype != ORC_BF16 && dtype != ORC_FP16)) return -1;
+#pragma omp parallel for schedule(static)
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    const uint16_t* g = (const uint16_t*)input + t * input_stride;
+    const uint16_t* u = g + d;
+    uint16_t* o = (uint16_t*)out + t * out_stride;
+    for (int64_t i = 0; i < d; ++i) {
+      const float gv = ld_act(&g[i], dtype);
+      const float e = (float)exp(-(double)gv);
+      const float s = gv / (1.0f + e);
+      o[i] = to_act(s * ld_act(&u[i], dtype), dtype);
+    }
+  }
+  return 0;
+}
+
+/* ---------------------------------------------------------------------------------------------
+ * Rotary embedding from the fp32 cos|sin cache. FI/data/include/flashinfer/pos_enc.cuh:129-147
+ * (neox: element i pairs with i + rotary_dim/2), :218-234 (interleaved: 2i pairs with 2i+1), cache
+ * row layout :375-391 (cos = cache[pos, i], sin = cache[pos, rotary_dim/2 + i]):
+ *   a' = a*cos - b*sin,  b' = b*cos + a*sin,  fp32, one rounding.
+ * Out-of-range positions leave the token as is and set bit 2 of *status.
+ * --------------------------------------------------------------------------------------------- */
+int orc_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, void* query,
+                                   void* key, const float* cache, int64_t num_tokens,
+                                   int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                                   int64_t rotary_dim, int64_t max_positions,
+                                   int64_t q_stride_token, int64_t q_stride_head,
+                                   int64_t k_stride_token, int64_t k_stride_head, int is_neox,
+                                   int dtype, int32_t* status) {
+  if (num_tokens < 0 || rotary_dim <= 0 || rotary_dim % 2 || rotary_dim > head_size) return -1;
+  if (dtype != ORC_BF16 && dtype != ORC_FP16) return -1;
+  const int64_t half = rotary_dim / 2;
+  int32_t flags = 0;
+#pragma omp parallel for schedule(static) reduction(| : flags)
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    const int64_t pos = positions_dtype == ORC_INT64 ? ((const int64_t*)positions)[t]
+                                                     : (int64_t)((const int32_t*)positions)[t];
+    if (pos < 0 || pos >= max_positions) { flags |= 2; continue; }
+    const float* c = cache + pos * rotary_dim;
+    const float* s = c + half;
+    for (int64_t h = 0; h < num_q_heads + num_kv_heads; ++h) {
+      uint16_t* p = h < num_q_heads
+                        ? (uint16_t*)query + t * q_stride_token + h * q_stride_head
+                        : (uint16_t*)key + t * k_stride_token + (h - num_q_heads) * k_stride_head;
+      for (int64_t i = 0; i < half; ++i) {
+        const int64_t i0 = is_neox ? i : 2 * i;
+        const int64_t i1 = is_neox ? i + half : 2 * i + 1;
+        const float a = ld_act(&p[i0], dtype), b = ld_act(&p[i1], dtype);
+        const float ac = a * c[i], bs = b * s[i], bc = b * c[i], as = a * s[i];
+        p[i0] = to_act(ac - bs, dtype);
+        p[i1] = to_act(bc + as, dtype);
+      }
+    }
+  }
+  if (status) *status |= flags;
+  return 0;
+}
+
+/* ---------------------------------------------------------------------------------------------
+ * Token-embedding gather: out[t] = table[ids[t]], a byte copy (torch.nn.functional.embedding).
+ * Out-of-range ids give a zero row and set bit 1 of *status.
+ * --------------------------------------------------------------------------------------------- */
+int orc_embedding_gather(void* out, const void* table, const void* ids, int ids_dtype,
+                         int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
+                         int64_t out_stride, int64_t table_stride, int elem_size, int32_t* status) {
+  if (num_tokens < 0 || hidden_size <= 0 || elem_size <= 0) return -1;
+  const size_t rb = (size_t)hidden_size * (size_t)elem_size;
+  int32_t flags = 0;
+#pragma omp parallel for schedule(static) reduction(| : flags)
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    const int64_t id = ids_dtype == ORC_INT64 ? ((const int64_t*)ids)[t]
+                                              : (int64_t)((const int32_t*)ids)[t];
+    unsigned char* dst = (unsigned char*)out + (size_t)t * (size_t)out_stride * (size_t)elem_size;
+    if (id < 0 || id >= vocab_size) { memset(dst, 0, rb); flags |= 1; continue; }
+    memcpy(dst, (const unsigned char*)table + (size_t)id * (size_t)table_stride * (size_t)elem_size, rb);
+  }
+  if (status) *status |= flags;
+  return 0;
+}

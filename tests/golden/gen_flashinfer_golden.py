@@ -1,0 +1,129 @@
+"""Generates golden fixtures from flashinfer 0.6.11.post2 -- the kernels the reference calls -- on a GPU.
+
+    python tests/golden/gen_flashinfer_golden.py [out_dir]      (needs a CUDA GPU and flashinfer)
+
+mini-agent-serve computes RMSNorm, SiLU-and-mul and rope through flashinfer (imports at
+miniagentserve/models/devstral2/devstral2.py:18-23). This script calls those same functions with the
+arguments the reference's call sites pass -- fused_add_rmsnorm (devstral2.py:305-307),
+fused_add_rmsnorm_quant (:241-252), silu_and_mul (:224), apply_rope_with_cos_sin_cache_inplace on
+strided q/k views of one qkv row (:158-166) -- on small seeded inputs, and saves inputs and outputs
+(bf16/fp16 as int16 bit patterns, e4m3 as uint8) to flashinfer_golden.npz. The CPU tests pin the
+oracle against these outputs; nothing in the product imports flashinfer.
+"""
+from __future__ import annotations
+
+import sys
+import traceback
+from pathlib import Path
+
+import numpy as np
+import torch
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu().contiguous()
+    if t.dtype in (torch.bfloat16, torch.float16):
+        return t.view(torch.int16).numpy()
+    if t.dtype == torch.float8_e4m3fn:
+        return t.view(torch.uint8).numpy()
+    return t.numpy()
+
+
+def main(out_dir: Path) -> None:
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cpu").manual_seed(20261201)
+    arrays: dict[str, np.ndarray] = {}
+    failures: list[str] = []
+
+    def rnd(*shape, scale=1.0, dtype=torch.bfloat16):
+        return (torch.randn(*shape, generator=g) * scale).to(dtype)
+
+    # ---- fused_add_rmsnorm (bf16 in place) ---------------------------------------------------
+    try:
+        from flashinfer.norm import fused_add_rmsnorm
+        for name, T, H, stride, dtype in (("n5120", 6, 5120, 5120, torch.bfloat16),
+                                           ("n12288", 3, 12288, 12288, torch.bfloat16),
+                                           ("n1000", 5, 1000, 1000, torch.bfloat16),
+                                           ("nstrided", 4, 2048, 3072, torch.bfloat16),
+                                           ("nfp16", 4, 4096, 4096, torch.float16)):
+            xb = rnd(T, stride, dtype=dtype)
+            rb = rnd(T, stride, scale=2.0, dtype=dtype)
+            w = (1 + 0.1 * torch.randn(H, generator=g)).to(dtype)
+            x_d, r_d = xb.to(dev), rb.to(dev)
+            fused_add_rmsnorm(x_d[:, :H], r_d[:, :H], w.to(dev), 1e-5, enable_pdl=True)
+            torch.cuda.synchronize()
+            arrays.update({f"norm_{name}_x": bits(xb), f"norm_{name}_r": bits(rb), f"norm_{name}_w": bits(w),
+                           f"norm_{name}_H": np.array(H), f"norm_{name}_xout": bits(x_d),
+                           f"norm_{name}_rout": bits(r_d), f"norm_{name}_dtype": np.array(str(dtype))})
+    except Exception:
+        failures.append("fused_add_rmsnorm: " + traceback.format_exc(limit=2))
+
+    # ---- fused_add_rmsnorm_quant (fp8 e4m3 out) -------------------------------------------------
+    try:
+        from flashinfer.norm import fused_add_rmsnorm_quant
+        for name, T, H, scale in (("q5120", 6, 5120, 0.05), ("q12288", 3, 12288, 0.005), ("q1000", 4, 1000, 0.5)):
+            xb = rnd(T, H)
+            rb = rnd(T, H)
+            w = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+            out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=dev)
+            x_d, r_d = xb.to(dev), rb.to(dev)
+            s = torch.tensor(scale, dtype=torch.float32, device=dev)
+            fused_add_rmsnorm_quant(out, x_d, r_d, w.to(dev), s, 1e-5, enable_pdl=True)
+            torch.cuda.synchronize()
+            arrays.update({f"quant_{name}_x": bits(xb), f"quant_{name}_r": bits(rb), f"quant_{name}_w": bits(w),
+                           f"quant_{name}_scale": np.array(scale, dtype=np.float32),
+                           f"quant_{name}_out": bits(out), f"quant_{name}_rout": bits(r_d),
+                           f"quant_{name}_xafter": bits(x_d)})
+    except Exception:
+        failures.append("fused_add_rmsnorm_quant: " + traceback.format_exc(limit=2))
+
+    # ---- silu_and_mul ------------------------------------------------------------------------------
+    try:
+        from flashinfer.activation import silu_and_mul
+        for name, T, d, scale, dtype in (("s4096", 4, 4096, 1.0, torch.bfloat16), ("s8", 3, 8, 1.0, torch.bfloat16),
+                                         ("swide", 2, 1024, 12.0, torch.bfloat16),
+                                         ("sfp16", 3, 1024, 3.0, torch.float16)):
+            xin = rnd(T, 2 * d, scale=scale, dtype=dtype)
+            out = silu_and_mul(xin.to(dev), enable_pdl=True)
+            torch.cuda.synchronize()
+            arrays.update({f"silu_{name}_in": bits(xin), f"silu_{name}_out": bits(out)})
+    except Exception:
+        failures.append("silu_and_mul: " + traceback.format_exc(limit=2))
+
+    # ---- apply_rope_with_cos_sin_cache_inplace -----------------------------------------------------
+    try:
+        from flashinfer.rope import apply_rope_with_cos_sin_cache_inplace
+        for name, T, Hq, Hkv, D, rd, P, neox, pdt in (("r128", 16, 4, 2, 128, 128, 64, True, torch.int32),
+                                                       ("r128i64", 9, 3, 1, 128, 128, 64, True, torch.int64),
+                                                       ("r64", 7, 2, 2, 64, 64, 32, True, torch.int32),
+                                                       ("rinter", 8, 2, 1, 128, 128, 64, False, torch.int32)):
+            width = (Hq + 2 * Hkv) * D
+            qkv = rnd(T, width)
+            ang = torch.rand(P, rd // 2, generator=g) * 6.283185307179586
+            cache = torch.cat([ang.cos(), ang.sin()], dim=-1).to(torch.float32)
+            pos = torch.randint(0, P, (T,), generator=g)
+            pos[0] = P - 1
+            pos = pos.to(pdt)
+            qkv_d = qkv.to(dev)
+            q, k = qkv_d[:, : Hq * D], qkv_d[:, Hq * D: (Hq + Hkv) * D]
+            apply_rope_with_cos_sin_cache_inplace(pos.to(dev), q, k, D, cache.to(dev), is_neox=neox)
+            torch.cuda.synchronize()
+            arrays.update({f"rope_{name}_qkv": bits(qkv), f"rope_{name}_cache": cache.numpy(),
+                           f"rope_{name}_pos": pos.numpy(), f"rope_{name}_out": bits(qkv_d),
+                           f"rope_{name}_dims": np.array([Hq, Hkv, D, int(neox)], dtype=np.int64)})
+    except Exception:
+        failures.append("apply_rope_with_cos_sin_cache_inplace: " + traceback.format_exc(limit=2))
+
+    import flashinfer
+    arrays["flashinfer_version"] = np.array(getattr(flashinfer, "__version__", "unknown"))
+    arrays["gpu"] = np.array(torch.cuda.get_device_name())
+    out_dir.mkdir(parents=True, exist_ok=True)
+    np.savez_compressed(out_dir / "flashinfer_golden.npz", **arrays)
+    (out_dir / "flashinfer_golden_failures.txt").write_text("\n".join(failures) or "none\n")
+    print("wrote", out_dir / "flashinfer_golden.npz", "failures:", len(failures))
+    for f in failures:
+        print(f)
+
+
+if __name__ == "__main__":
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path(__file__).resolve().parent)

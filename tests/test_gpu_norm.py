@@ -1,0 +1,136 @@
+"""Parity of the fused add RMSNorm kernels (bf16/fp16 in place, and e4m3 out) against the oracle.
+
+The residual (an fp32 sum of two 16-bit values, rounded once) must be bit-exact; the normalised
+output within 1 ulp (bf16/fp16) or 1 e4m3 step. Cases cover the TMA ring path (H % 8 == 0, aligned
+rows: 1000 to 24576), the generic path (odd H, unaligned strides, H beyond the ring's limit), strided
+rows, empty and single-token batches, and configuration 1 at full size.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import mas_b200
+import oracle
+from mas_b200 import workloads
+from parity import assert_bits_equal, assert_ulp
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(T, H, dtype, stride=None, seed=0, rscale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    stride = H if stride is None else stride
+    xb = torch.randn(T, stride, generator=g).to(dtype)
+    rb = (torch.randn(T, stride, generator=g) * rscale).to(dtype)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).to(dtype)
+    return xb, rb, w
+
+
+def _run_bf16(cuda, T, H, dtype=torch.bfloat16, stride=None, eps=1e-5, rscale=1.0):
+    xb, rb, w = _inputs(T, H, dtype, stride, rscale=rscale)
+    xd, rd = xb.to(cuda), rb.to(cuda)
+    mas_b200.fused_add_rmsnorm(xd[:, :H], rd[:, :H], w.to(cuda), eps)
+    xo, ro = xb.clone(), rb.clone()
+    oracle.fused_add_rmsnorm(xo[:, :H], ro[:, :H], w, eps)
+    torch.cuda.synchronize()
+    assert_bits_equal(rd.cpu(), ro, "residual")
+    return assert_ulp(xd.cpu(), xo, what=f"norm T={T} H={H} stride={stride}")
+
+
+@pytest.mark.parametrize("T,H", [(1, 5120), (7, 5120), (33, 12288), (5, 1000), (300, 4096), (2, 16384),
+                                 (3, 24576), (64, 128), (9, 8)])
+def test_norm_fast_path(cuda, T, H):
+    _run_bf16(cuda, T, H)
+
+
+@pytest.mark.parametrize("T,H", [(3, 1001), (4, 7), (2, 32768), (1, 65536), (5, 12)])
+def test_norm_generic_path(cuda, T, H):
+    _run_bf16(cuda, T, H)
+
+
+@pytest.mark.parametrize("stride", [10240, 5124, 5128])
+def test_norm_strided_rows(cuda, stride):
+    _run_bf16(cuda, 6, 5120, stride=stride)
+
+
+def test_norm_fp16(cuda):
+    _run_bf16(cuda, 17, 4096, dtype=torch.float16)
+
+
+def test_norm_large_residual(cuda):
+    _run_bf16(cuda, 8, 5120, rscale=300.0)
+
+
+def test_norm_empty(cuda):
+    x = torch.empty(0, 5120, dtype=torch.bfloat16, device=cuda)
+    r = torch.empty_like(x)
+    mas_b200.fused_add_rmsnorm(x, r, torch.ones(5120, dtype=torch.bfloat16, device=cuda), 1e-5)
+    torch.cuda.synchronize()
+
+
+def test_norm_config1_full(cuda):
+    """Configuration 1: x, r ~ N(0,1) bf16 [4096, 5120], w = 1 + 0.1 N(0,1), eps 1e-5, seed 0."""
+    x, r, w, eps = workloads.norm_inputs(cuda)
+    xo, ro = x.cpu(), r.cpu()
+    mas_b200.fused_add_rmsnorm(x, r, w, eps)
+    oracle.fused_add_rmsnorm(xo, ro, w.cpu(), eps)
+    assert_bits_equal(r, ro, "residual")
+    assert_ulp(x, xo, what="config 1")
+
+
+def test_norm_repeat_deterministic(cuda):
+    xb, rb, w = _inputs(129, 5120, torch.bfloat16)
+    outs = []
+    for _ in range(2):
+        xd, rd = xb.to(cuda), rb.to(cuda)
+        mas_b200.fused_add_rmsnorm(xd, rd, w.to(cuda), 1e-5)
+        outs.append((xd.cpu(), rd.cpu()))
+    assert_bits_equal(outs[0][0], outs[1][0], "x run-to-run")
+    assert_bits_equal(outs[0][1], outs[1][1], "r run-to-run")
+
+
+@pytest.mark.parametrize("T,H,scale", [(6, 5120, 0.05), (3, 12288, 0.005), (4, 1000, 0.5), (5, 1001, 0.05),
+                                       (2, 32768, 0.05), (1, 8, 1.0)])
+def test_norm_quant(cuda, T, H, scale):
+    xb, rb, w = _inputs(T, H, torch.bfloat16)
+    out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=cuda)
+    xd, rd = xb.to(cuda), rb.to(cuda)
+    mas_b200.fused_add_rmsnorm_quant(out, xd, rd, w.to(cuda), torch.tensor([scale], device=cuda), 1e-5)
+    oo = torch.empty(T, H, dtype=torch.float8_e4m3fn)
+    xo, ro = xb.clone(), rb.clone()
+    oracle.fused_add_rmsnorm_quant(oo, xo, ro, w, scale, 1e-5)
+    assert_bits_equal(xd.cpu(), xb, "input left unchanged")
+    assert_bits_equal(rd.cpu(), ro, "residual")
+    assert_ulp(out.cpu(), oo, what=f"fp8 out T={T} H={H}")
+
+
+def test_norm_quant_scalar_scale_and_strided_out(cuda):
+    T, H = 4, 2048
+    xb, rb, w = _inputs(T, H, torch.bfloat16)
+    big = torch.zeros(T, 4096, dtype=torch.float8_e4m3fn, device=cuda)
+    out = big[:, :H]
+    xd, rd = xb.to(cuda), rb.to(cuda)
+    mas_b200.fused_add_rmsnorm_quant(out, xd, rd, w.to(cuda), torch.tensor(0.25, device=cuda), 1e-5)
+    oo = torch.empty(T, H, dtype=torch.float8_e4m3fn)
+    xo, ro = xb.clone(), rb.clone()
+    oracle.fused_add_rmsnorm_quant(oo, xo, ro, w, 0.25, 1e-5)
+    assert_ulp(out.cpu(), oo, what="strided fp8 out")
+    assert torch.count_nonzero(big[:, H:].view(torch.uint8)) == 0
+
+
+def test_norm_c_abi_direct(cuda):
+    """The C ABI called with raw pointers, strides and the current stream."""
+    T, H = 5, 5120
+    xb, rb, w = _inputs(T, H, torch.bfloat16)
+    xd, rd, wd = xb.to(cuda), rb.to(cuda), w.to(cuda)
+    lib = mas_b200._lib.lib
+    rc = lib.mas_fused_add_rmsnorm(xd.data_ptr(), rd.data_ptr(), wd.data_ptr(), T, H, H, H, 1e-5, 0, 0,
+                                   torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, mas_b200.status_string(rc)
+    xo, ro = xb.clone(), rb.clone()
+    oracle.fused_add_rmsnorm(xo, ro, w, 1e-5)
+    assert_ulp(xd.cpu(), xo, what="C ABI")
+    assert lib.mas_fused_add_rmsnorm(xd.data_ptr(), rd.data_ptr(), wd.data_ptr(), T, H, H - 1, H, 1e-5, 0, 0, None) == -1
+    assert lib.mas_fused_add_rmsnorm(xd.data_ptr(), rd.data_ptr(), wd.data_ptr(), T, H, H, H, 1e-5, 7, 0, None) == -2
+    assert mas_b200.read_fault_word(0) == 0
