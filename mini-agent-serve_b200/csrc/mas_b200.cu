@@ -199,12 +199,14 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
     const size_t stage = 2ull * (size_t)H * sizeof(T);
     static const int env_ctas = env_int("MAS_NORM_CTAS_PER_SM", 0);
     static const int env_stages = env_int("MAS_NORM_STAGES", 0);
-    // CTAs per SM: as many as threads allow while each keeps at least a 2-stage ring.
-    int ctas = (int)std::min<int64_t>(2048 / nt, (int64_t)(kRingBytesPerSm / (2 * stage)));
-    if (env_ctas > 0) ctas = env_ctas;
-    if (ctas < 1) ctas = 1;
-    int stages = (int)(kRingBytesPerSm / ((size_t)ctas * stage));
-    if (env_stages > 0) stages = env_stages;
+    // Ring depth first: a stage is refilled one row after it is consumed, so S stages keep S-1 rows
+    // in flight per CTA; 4 stages hide the load latency behind three rows of work. Then as many CTAs
+    // per SM as the ring budget and the thread limit allow, and any budget left deepens the ring.
+    int stages = env_stages > 0 ? env_stages : 4;
+    if ((size_t)stages * stage > kRingBytesPerSm) stages = (int)std::max<size_t>(2, kRingBytesPerSm / stage);
+    int ctas = env_ctas > 0 ? env_ctas : (int)std::max<size_t>(1, kRingBytesPerSm / ((size_t)stages * stage));
+    ctas = std::max(1, std::min(ctas, 2048 / nt));
+    if (env_stages <= 0) stages = (int)std::max<size_t>(stages, std::min<size_t>(8, kRingBytesPerSm / ((size_t)ctas * stage)));
     stages = std::max(2, std::min(8, stages));
     const size_t smem = norm_tma_smem_bytes(H, stages, (int)sizeof(T));
     const void* fn = norm_tma_fn<T, Q>(vpt);
@@ -393,7 +395,7 @@ int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, v
   if (vec) {
     a.tpu = (int32_t)(rotary_dim / 16);
     const int64_t upb = kRopeThreads / a.tpu;
-    const dim3 grid((unsigned)std::min<int64_t>(ceil_div(num_tokens * NH, upb), INT32_MAX));
+    const dim3 grid((unsigned)std::min<int64_t>(ceil_div(num_tokens * NH, upb * kRopeUnits), INT32_MAX));
     MAS_ROPE_LAUNCH(rope_vec_kernel, grid);
   }
   const int64_t pairs = num_tokens * NH * (rotary_dim / 2);

@@ -9,8 +9,10 @@
 // owns the 8 pairs whose cos/sin are cache[pos, 8j .. 8j+8), so each thread does exactly two
 // 16-byte loads and two 16-byte stores of q/k (both halves of its pairs) plus four 16-byte cos/sin
 // loads that hit L1 for all heads of a token after the first. Units run token-major, heads of one
-// token adjacent, so q and k of a token stream through together. q and k may be strided views of
-// one fused qkv row (Devstral2Attention.forward, miniagentserve/models/devstral2/devstral2.py:158).
+// token adjacent, so q and k of a token stream through together, and each thread group takes two
+// adjacent units per iteration with all four q/k loads in flight before any position is examined.
+// q and k may be strided views of one fused qkv row (Devstral2Attention.forward,
+// miniagentserve/models/devstral2/devstral2.py:158).
 #pragma once
 
 #include "common.cuh"
@@ -42,6 +44,21 @@ __device__ __forceinline__ void load_f8(const float* p, float (&f)[8]) {
   f[6] = __uint_as_float(b.c); f[7] = __uint_as_float(b.d);
 }
 
+// The rotation of one pair, evaluated as flashinfer's compiled kernel does (pos_enc.cuh:129-147
+// and :218-234 contract to one fused multiply-add with a separately rounded second product):
+//   a' = fma(a, c, -(b*s)),  b' = fma(b, c, a*s).
+// Written with explicit intrinsics so the result does not depend on the compiler's contraction.
+__device__ __forceinline__ void rotate(float a, float b, float c, float s, float& ra, float& rb) {
+  ra = __fmaf_rn(a, c, -__fmul_rn(b, s));
+  rb = __fmaf_rn(b, c, __fmul_rn(a, s));
+}
+
+// Each thread group handles kRopeUnits adjacent units per iteration (usually heads of one token,
+// so the position and the cos/sin row are shared). All q/k loads of the iteration are issued before
+// the position is checked: a load never waits on another load's latency, and a position out of
+// range only suppresses the stores.
+constexpr int kRopeUnits = 2;
+
 template <typename T, typename PosT, bool NEOX>
 __global__ void __launch_bounds__(kRopeThreads) rope_vec_kernel(const RopeArgs a) {
   pdl_wait();
@@ -54,53 +71,55 @@ __global__ void __launch_bounds__(kRopeThreads) rope_vec_kernel(const RopeArgs a
     const uint32_t units = (uint32_t)a.T * NH;  // host guarantees < 2^31
     const int half = a.rd >> 1;
     const PosT* pos_p = static_cast<const PosT*>(a.pos);
-    for (uint32_t u = blockIdx.x * (uint32_t)upb + (uint32_t)g; u < units;
-         u += gridDim.x * (uint32_t)upb) {
-      const uint32_t t = u / NH;
-      const uint32_t h = u - t * NH;
-      const int64_t pos = (int64_t)pos_p[t];
-      if (pos < 0 || pos >= a.P) {
-        if (j == 0 && h == 0) flag_status(a.status, MAS_STATUS_ROPE_POS_OUT_OF_RANGE);
-        continue;
+    // element offsets of this thread's two 16-byte vectors within a head
+    const int off0 = NEOX ? j * 8 : j * 16;
+    const int off1 = NEOX ? half + j * 8 : j * 16 + 8;
+    const uint32_t stride = gridDim.x * (uint32_t)upb * kRopeUnits;
+    for (uint32_t u0 = (blockIdx.x * (uint32_t)upb + (uint32_t)g) * kRopeUnits; u0 < units; u0 += stride) {
+      T* ptr[kRopeUnits];
+      uint32_t tok[kRopeUnits];
+      Vec16 v0[kRopeUnits], v1[kRopeUnits];
+#pragma unroll
+      for (int i = 0; i < kRopeUnits; ++i) {
+        const uint32_t u = u0 + i;
+        ptr[i] = nullptr;
+        if (u < units) {
+          const uint32_t t = u / NH;
+          const uint32_t h = u - t * NH;
+          tok[i] = t;
+          ptr[i] = (h < (uint32_t)a.Hq)
+                       ? static_cast<T*>(a.q) + (int64_t)t * a.qsn + (int64_t)h * a.qsh
+                       : static_cast<T*>(a.k) + (int64_t)t * a.ksn + (int64_t)(h - a.Hq) * a.ksh;
+          v0[i] = ld_plain(ptr[i] + off0);
+          v1[i] = ld_plain(ptr[i] + off1);
+        }
       }
-      const float* c = a.cache + pos * a.rd;
-      T* p = (h < (uint32_t)a.Hq)
-                 ? static_cast<T*>(a.q) + (int64_t)t * a.qsn + (int64_t)h * a.qsh
-                 : static_cast<T*>(a.k) + (int64_t)t * a.ksn + (int64_t)(h - a.Hq) * a.ksh;
-      float cs[8], sn[8];
-      load_f8(c + j * 8, cs);
-      load_f8(c + half + j * 8, sn);
-      if constexpr (NEOX) {
-        T* plo = p + j * 8;
-        T* phi = p + half + j * 8;
-        const Vec16 lo = ld_plain(plo);
-        const Vec16 hi = ld_plain(phi);
-        float xl[8], xh[8], ol[8], oh[8];
-        unpack8<T>(lo, xl);
-        unpack8<T>(hi, xh);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          ol[e] = xl[e] * cs[e] - xh[e] * sn[e];
-          oh[e] = xh[e] * cs[e] + xl[e] * sn[e];
+      for (int i = 0; i < kRopeUnits; ++i) {
+        if (ptr[i] == nullptr) continue;
+        const int64_t pos = (int64_t)pos_p[tok[i]];
+        if (pos < 0 || pos >= a.P) {
+          if (j == 0) flag_status(a.status, MAS_STATUS_ROPE_POS_OUT_OF_RANGE);
+          continue;
         }
-        st_plain(plo, pack8<T>(ol));
-        st_plain(phi, pack8<T>(oh));
-      } else {
-        T* p0 = p + j * 16;
-        const Vec16 v0 = ld_plain(p0);
-        const Vec16 v1 = ld_plain(p0 + 8);
-        float x0[8], x1[8], o0[8], o1[8];
-        unpack8<T>(v0, x0);
-        unpack8<T>(v1, x1);
+        const float* c = a.cache + pos * a.rd;
+        float cs[8], sn[8], x0[8], x1[8], o0[8], o1[8];
+        load_f8(c + j * 8, cs);
+        load_f8(c + half + j * 8, sn);
+        unpack8<T>(v0[i], x0);
+        unpack8<T>(v1[i], x1);
+        if constexpr (NEOX) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          o0[2 * e] = x0[2 * e] * cs[e] - x0[2 * e + 1] * sn[e];
-          o0[2 * e + 1] = x0[2 * e + 1] * cs[e] + x0[2 * e] * sn[e];
-          o1[2 * e] = x1[2 * e] * cs[4 + e] - x1[2 * e + 1] * sn[4 + e];
-          o1[2 * e + 1] = x1[2 * e + 1] * cs[4 + e] + x1[2 * e] * sn[4 + e];
+          for (int e = 0; e < 8; ++e) rotate(x0[e], x1[e], cs[e], sn[e], o0[e], o1[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            rotate(x0[2 * e], x0[2 * e + 1], cs[e], sn[e], o0[2 * e], o0[2 * e + 1]);
+            rotate(x1[2 * e], x1[2 * e + 1], cs[4 + e], sn[4 + e], o1[2 * e], o1[2 * e + 1]);
+          }
         }
-        st_plain(p0, pack8<T>(o0));
-        st_plain(p0 + 8, pack8<T>(o1));
+        st_plain(ptr[i] + off0, pack8<T>(o0));
+        st_plain(ptr[i] + off1, pack8<T>(o1));
       }
     }
   }
@@ -133,10 +152,10 @@ __global__ void __launch_bounds__(kRopeThreads) rope_generic_kernel(const RopeAr
                       : static_cast<uint16_t*>(a.k) + t * a.ksn + (h - a.Hq) * a.ksh;
     const int64_t i0 = NEOX ? i : 2 * i;
     const int64_t i1 = NEOX ? i + half : 2 * i + 1;
-    const float x0 = Elem<T>::to_f(p[i0]);
-    const float x1 = Elem<T>::to_f(p[i1]);
-    p[i0] = Elem<T>::from_f(x0 * c - x1 * s);
-    p[i1] = Elem<T>::from_f(x1 * c + x0 * s);
+    float r0, r1;
+    rotate(Elem<T>::to_f(p[i0]), Elem<T>::to_f(p[i1]), c, s, r0, r1);
+    p[i0] = Elem<T>::from_f(r0);
+    p[i1] = Elem<T>::from_f(r1);
   }
   pdl_launch_dependents();
 }

@@ -191,7 +191,9 @@ int orc_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
  * Rotary embedding from the fp32 cos|sin cache. FI/data/include/flashinfer/pos_enc.cuh:129-147
  * (neox: element i pairs with i + rotary_dim/2), :218-234 (interleaved: 2i pairs with 2i+1), cache
  * row layout :375-391 (cos = cache[pos, i], sin = cache[pos, rotary_dim/2 + i]):
- *   a' = a*cos - b*sin,  b' = b*cos + a*sin,  fp32, one rounding.
+ *   a' = a*cos - b*sin,  b' = b*cos + a*sin,  rounded once to the output type,
+ * each evaluated as flashinfer's compiled kernel evaluates `x*cos + (+-y)*sin`: the second product
+ * rounded to fp32, then one fused multiply-add (fmaf, exact before its single rounding).
  * Out-of-range positions leave the token as is and set bit 2 of *status.
  * --------------------------------------------------------------------------------------------- */
 int orc_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, void* query,
@@ -220,9 +222,9 @@ int orc_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, v
         const int64_t i0 = is_neox ? i : 2 * i;
         const int64_t i1 = is_neox ? i + half : 2 * i + 1;
         const float a = ld_act(&p[i0], dtype), b = ld_act(&p[i1], dtype);
-        const float ac = a * c[i], bs = b * s[i], bc = b * c[i], as = a * s[i];
-        p[i0] = to_act(ac - bs, dtype);
-        p[i1] = to_act(bc + as, dtype);
+        const float bs = b * s[i], as = a * s[i];
+        p[i0] = to_act(fmaf(a, c[i], -bs), dtype);
+        p[i1] = to_act(fmaf(b, c[i], as), dtype);
       }
     }
   }

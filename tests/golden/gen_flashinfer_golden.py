@@ -111,6 +111,36 @@ def main(out_dir: Path) -> None:
             arrays.update({f"rope_{name}_qkv": bits(qkv), f"rope_{name}_cache": cache.numpy(),
                            f"rope_{name}_pos": pos.numpy(), f"rope_{name}_out": bits(qkv_d),
                            f"rope_{name}_dims": np.array([Hq, Hkv, D, int(neox)], dtype=np.int64)})
+        # Near-cancellation pairs: partners chosen so that a*cos - b*sin (or b*cos + a*sin) nearly
+        # vanishes, which exposes how the kernel's fp32 expression is evaluated (fused multiply-add
+        # or two rounded products).
+        for name, neox in (("rcancel", True), ("rcancel_inter", False)):
+            T, Hq, Hkv, D, P = 24, 4, 2, 128, 64
+            half = D // 2
+            ang = torch.rand(P, half, generator=g) * 6.283185307179586
+            cache = torch.cat([ang.cos(), ang.sin()], dim=-1).to(torch.float32)
+            pos = torch.randint(0, P, (T,), generator=g)
+            heads = torch.randn(T, Hq + Hkv, D, generator=g, dtype=torch.float64)
+            c = cache[pos][:, None, :half].double()
+            s = cache[pos][:, None, half:].double()
+            a = heads[..., :half] if neox else heads[..., 0::2]
+            sel = torch.rand(a.shape, generator=g) < 0.5
+            b = torch.where(sel, a * c / s, -a * s / c)  # first or second output nearly cancels
+            b = b.clamp(-64, 64)
+            if neox:
+                heads[..., half:] = b
+            else:
+                heads[..., 1::2] = b
+            qkv = torch.cat([heads.reshape(T, -1), torch.randn(T, Hkv * D, generator=g, dtype=torch.float64)], dim=1)
+            qkv = qkv.to(torch.bfloat16)
+            pos = pos.to(torch.int32)
+            qkv_d = qkv.to(dev)
+            q, k = qkv_d[:, : Hq * D], qkv_d[:, Hq * D: (Hq + Hkv) * D]
+            apply_rope_with_cos_sin_cache_inplace(pos.to(dev), q, k, D, cache.to(dev), is_neox=neox)
+            torch.cuda.synchronize()
+            arrays.update({f"rope_{name}_qkv": bits(qkv), f"rope_{name}_cache": cache.numpy(),
+                           f"rope_{name}_pos": pos.numpy(), f"rope_{name}_out": bits(qkv_d),
+                           f"rope_{name}_dims": np.array([Hq, Hkv, D, int(neox)], dtype=np.int64)})
     except Exception:
         failures.append("apply_rope_with_cos_sin_cache_inplace: " + traceback.format_exc(limit=2))
 

@@ -1,0 +1,141 @@
+"""The C oracle against a second, independent restatement in torch on the CPU (small cases).
+
+Two restatements of flashinfer's arithmetic written separately -- the C one (oracle/oracle.c, used as
+the checker of the GPU kernels) and the torch one below (fp32 elementwise ops, each rounded; the
+rope's one fused multiply-add evaluated exactly in float64) -- must agree: bit-exact for the gather
+and the residual, <= 1 ulp for the rest (they differ only in how the sum of squares and exp are
+accumulated). This guards the oracle's indexing:
+strides, leading dimensions, neox vs interleaved pairs, partial rotary, int32/int64 indices.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import oracle
+from parity import assert_bits_equal, assert_ulp
+
+
+def torch_norm(x, r, w, eps, scale=None):
+    h = x.float() + r.float()
+    rstd = (1.0 / torch.sqrt(h.double().pow(2).mean(-1, keepdim=True) + eps)).float()
+    y = h * rstd * w.float()
+    if scale is not None:
+        return (y * (1.0 / torch.tensor(scale, dtype=torch.float32))).clamp(-448, 448).to(torch.float8_e4m3fn), h.to(x.dtype)
+    return y.to(x.dtype), h.to(x.dtype)
+
+
+def torch_silu(x):
+    d = x.shape[-1] // 2
+    g, u = x[..., :d].float(), x[..., d:].float()
+    e = torch.exp(-g.double()).float()
+    return (g / (1.0 + e) * u).to(x.dtype)
+
+
+def torch_rope(pos, q, k, D, cache, neox=True):
+    rd = cache.shape[1]
+    half = rd // 2
+    out = []
+    for t in (q, k):
+        v = t.view(t.shape[0], -1, D).float().clone()
+        c = cache[pos.long()][:, None, :half]
+        s = cache[pos.long()][:, None, half:]
+        if neox:
+            a, b = v[..., :half].clone(), v[..., half:rd].clone()
+        else:
+            a, b = v[..., 0:rd:2].clone(), v[..., 1:rd:2].clone()
+        # one fused multiply-add after a rounded second product (evaluated exactly in float64)
+        na = (a.double() * c.double() - (b * s).double()).float()
+        nb = (b.double() * c.double() + (a * s).double()).float()
+        if neox:
+            v[..., :half], v[..., half:rd] = na, nb
+        else:
+            v[..., 0:rd:2], v[..., 1:rd:2] = na, nb
+        out.append(v.to(t.dtype).view(t.shape))
+    return out
+
+
+@pytest.mark.parametrize("T,H,dtype", [(5, 64, torch.bfloat16), (3, 1000, torch.bfloat16), (4, 96, torch.float16)])
+def test_norm(T, H, dtype):
+    g = torch.Generator().manual_seed(T * H)
+    x, r = torch.randn(T, H, generator=g).to(dtype), (torch.randn(T, H, generator=g) * 3).to(dtype)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).to(dtype)
+    y_t, r_t = torch_norm(x, r, w, 1e-5)
+    xo, ro = x.clone(), r.clone()
+    oracle.fused_add_rmsnorm(xo, ro, w, 1e-5)
+    assert_bits_equal(ro, r_t, "residual")
+    assert_ulp(xo, y_t, what="norm")
+
+
+def test_norm_strided_rows():
+    g = torch.Generator().manual_seed(3)
+    big_x, big_r = torch.randn(4, 300, generator=g).to(torch.bfloat16), torch.randn(4, 300, generator=g).to(torch.bfloat16)
+    w = torch.randn(128, generator=g).to(torch.bfloat16)
+    y_t, r_t = torch_norm(big_x[:, :128], big_r[:, :128], w, 1e-6)
+    xo, ro = big_x.clone(), big_r.clone()
+    oracle.fused_add_rmsnorm(xo[:, :128], ro[:, :128], w, 1e-6)
+    assert_ulp(xo[:, :128], y_t, what="strided norm")
+    assert_bits_equal(ro[:, :128], r_t, "strided residual")
+    assert_bits_equal(xo[:, 128:], big_x[:, 128:], "outside the rows")
+
+
+@pytest.mark.parametrize("scale", [0.5, 0.01])
+def test_norm_quant(scale):
+    g = torch.Generator().manual_seed(4)
+    x, r = torch.randn(6, 256, generator=g).to(torch.bfloat16), torch.randn(6, 256, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(256, generator=g)).to(torch.bfloat16)
+    y_t, r_t = torch_norm(x, r, w, 1e-5, scale=scale)
+    out = torch.empty(6, 256, dtype=torch.float8_e4m3fn)
+    xo, ro = x.clone(), r.clone()
+    oracle.fused_add_rmsnorm_quant(out, xo, ro, w, scale, 1e-5)
+    assert_bits_equal(xo, x, "input unchanged")
+    assert_bits_equal(ro, r_t, "residual")
+    assert_ulp(out, y_t, what="fp8")
+
+
+@pytest.mark.parametrize("shape,scale", [((7, 64), 1.0), ((2, 3, 40), 5.0), ((4, 16), 100.0)])
+def test_silu(shape, scale):
+    x = (torch.randn(*shape, generator=torch.Generator().manual_seed(5)) * scale).to(torch.bfloat16)
+    assert_ulp(oracle.silu_and_mul(x.reshape(-1, shape[-1])).view(*shape[:-1], shape[-1] // 2), torch_silu(x),
+               what="silu")
+
+
+@pytest.mark.parametrize("D,rd,neox,pdt", [(128, 128, True, torch.int32), (128, 128, False, torch.int64),
+                                           (64, 32, True, torch.int32), (40, 40, False, torch.int32)])
+def test_rope(D, rd, neox, pdt):
+    g = torch.Generator().manual_seed(D + rd)
+    T, Hq, Hkv, P = 9, 3, 2, 50
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, generator=g).to(torch.bfloat16)
+    ang = torch.rand(P, rd // 2, generator=g) * 6.28
+    cache = torch.cat([ang.cos(), ang.sin()], -1)
+    pos = torch.randint(0, P, (T,), generator=g).to(pdt)
+    q, k = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D]
+    qt, kt = torch_rope(pos, q, k, D, cache, neox)
+    qo = qkv.clone()
+    st = oracle.apply_rope_with_cos_sin_cache_inplace(pos, qo[:, : Hq * D], qo[:, Hq * D: (Hq + Hkv) * D], D, cache,
+                                                      is_neox=neox)
+    assert st == 0
+    assert_ulp(qo[:, : Hq * D], qt, what="q")
+    assert_ulp(qo[:, Hq * D: (Hq + Hkv) * D], kt, what="k")
+    assert_bits_equal(qo[:, (Hq + Hkv) * D:], qkv[:, (Hq + Hkv) * D:], "v untouched")
+
+
+def test_rope_out_of_range_position_untouched():
+    qkv = torch.randn(3, 3 * 64).to(torch.bfloat16)
+    cache = torch.randn(10, 64)
+    pos = torch.tensor([0, 10, -1], dtype=torch.int32)
+    qo = qkv.clone()
+    st = oracle.apply_rope_with_cos_sin_cache_inplace(pos, qo[:, :128], qo[:, 128:], 64, cache)
+    assert st == 2
+    assert_bits_equal(qo[1:], qkv[1:], "bad positions untouched")
+
+
+def test_embedding_out_of_range_and_dtypes():
+    table = torch.randn(20, 6)
+    ids = torch.tensor([[3, 19], [0, 20]], dtype=torch.int64)
+    out, st = oracle.embedding(ids, table)
+    assert st == 1
+    assert torch.equal(out[0, 0], table[3]) and torch.equal(out[0, 1], table[19]) and torch.equal(out[1, 0], table[0])
+    assert torch.count_nonzero(out[1, 1]) == 0
+    out32, st32 = oracle.embedding(ids[0].to(torch.int32), table.to(torch.bfloat16))
+    assert st32 == 0 and torch.equal(out32, table.to(torch.bfloat16)[ids[0]])
