@@ -11,6 +11,7 @@ from pathlib import Path
 
 _PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("MAS_B200_LIB", str(_PKG / "libmas_b200.so")))
+TORCH_LIB_PATH = _PKG / "libmas_b200_torch.so"
 
 # Dtype codes (MAS_DTYPE_*).
 DTYPE_BF16 = 0
@@ -67,6 +68,19 @@ def _load() -> ctypes.CDLL:
 
 
 lib = _load()
+
+
+def _load_torch_ops() -> None:
+    """Registers the `mas_b200::*` operators (C++, over the C ABI) with the torch dispatcher."""
+    import torch
+
+    if not TORCH_LIB_PATH.exists():
+        raise ImportError(f"mas_b200: operator library {TORCH_LIB_PATH} is missing. Build it with "
+                          f"`python {_PKG / 'build.py'}`.")
+    torch.ops.load_library(str(TORCH_LIB_PATH))
+
+
+_load_torch_ops()
 
 
 class MasError(RuntimeError):

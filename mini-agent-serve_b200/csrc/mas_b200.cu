@@ -66,6 +66,8 @@ cudaError_t prepare_current(DeviceState& st, int device) {
   if ((e = opt_in_norm<__nv_bfloat16, true>()) != cudaSuccess) return e;
   if ((e = opt_in_norm<__half, false>()) != cudaSuccess) return e;
   if ((e = opt_in_norm<__half, true>()) != cudaSuccess) return e;
+  if ((e = opt_in_smem(silu_mul_ring_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(silu_mul_ring_kernel<__half>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(embed_tma_kernel<int32_t>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(embed_tma_kernel<int64_t>)) != cudaSuccess) return e;
   void* fault = nullptr;
@@ -194,8 +196,8 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
   const int H = a.H;
   if (fast_ok && H % 8 == 0) {
     const int nv = H / 8;
-    const int vpt = (int)ceil_div(nv, 512);
-    const int nt = (int)ceil_div(ceil_div(nv, vpt), 32) * 32;
+    const int vpt = (int)ceil_div(nv, kNormMaxConsumers);
+    const int nt = 32 + (int)ceil_div(ceil_div(nv, vpt), 32) * 32;  // producer warp + consumers
     const size_t stage = 2ull * (size_t)H * sizeof(T);
     static const int env_ctas = env_int("MAS_NORM_CTAS_PER_SM", 0);
     static const int env_stages = env_int("MAS_NORM_STAGES", 0);
@@ -326,18 +328,30 @@ int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
   if (rc != MAS_OK) return rc;
   SiluArgs a = {};
   a.out = out; a.in = input; a.rows = num_tokens; a.in_stride = input_stride;
-  a.out_stride = out_stride; a.d = (int32_t)d;
-  const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, 65535);
-  const bool vec = d % 8 == 0 && aligned(out, 16) && aligned(input, 16) && input_stride % 8 == 0 &&
-                   out_stride % 8 == 0;
-  if (vec) {
-    constexpr int U = 4;
-    const int64_t nvec = d / 8;
-    const unsigned gx = (unsigned)ceil_div(nvec, kSiluThreads * U);
-    if (dtype == MAS_DTYPE_BF16)
-      return launch(silu_mul_vec_kernel<__nv_bfloat16, U>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
-    return launch(silu_mul_vec_kernel<__half, U>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+  a.out_stride = out_stride; a.d = (int32_t)d; a.fault = st->fault;
+  const bool ring = d % 8 == 0 && aligned(out, 16) && aligned(input, 16) && input_stride % 8 == 0 &&
+                    out_stride % 8 == 0;
+  if (ring) {
+    static const int env_stages = env_int("MAS_SILU_STAGES", 0);
+    static const int env_ctas = env_int("MAS_SILU_CTAS_PER_SM", 0);
+    const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 6));
+    const size_t smem = silu_ring_smem_bytes(stages, 2);
+    int ctas = env_ctas > 0 ? env_ctas : (int)std::max<size_t>(1, kRingBytesPerSm / smem);
+    const void* fn = dtype == MAS_DTYPE_BF16 ? (const void*)silu_mul_ring_kernel<__nv_bfloat16>
+                                             : (const void*)silu_mul_ring_kernel<__half>;
+    ctas = std::min(ctas, resident_ctas(fn, kSiluRingThreads, smem));
+    const int64_t tiles = num_tokens * ceil_div(d, kSiluChunk);
+    int64_t grid = std::min<int64_t>(tiles, (int64_t)st->sm_count * ctas);
+    a.tiles_per_cta = ceil_div(tiles, grid);
+    grid = ceil_div(tiles, a.tiles_per_cta);
+    a.stages = stages;
+    if (smem <= kMaxSmemPerCta) {
+      if (dtype == MAS_DTYPE_BF16)
+        return launch(silu_mul_ring_kernel<__nv_bfloat16>, dim3((unsigned)grid), dim3(kSiluRingThreads), smem, stream, enable_pdl, a);
+      return launch(silu_mul_ring_kernel<__half>, dim3((unsigned)grid), dim3(kSiluRingThreads), smem, stream, enable_pdl, a);
+    }
   }
+  const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, 65535);
   const unsigned gx = (unsigned)std::min<int64_t>(ceil_div(d, kSiluThreads), 1 << 16);
   if (dtype == MAS_DTYPE_BF16)
     return launch(silu_mul_generic_kernel<__nv_bfloat16>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);

@@ -6,13 +6,15 @@
 // and the norm is taken over the UNROUNDED h: y = h * rsqrt(sum(h^2)/H + eps) * w, rounded once.
 // The e4m3 variant multiplies by 1/scale, clamps to +-448 and rounds to nearest even.
 //
-// Fast path (rows of H % 8 == 0 elements, 16-byte aligned rows): a persistent grid. Each CTA owns
-// a contiguous block of rows and runs an S-stage ring in shared memory; thread 0 streams whole rows
-// of x and r into the ring with TMA bulk copies (cp.async.bulk, mbarrier transaction counts), so
-// several rows per SM are always in flight. Each thread owns the same VPT 16-byte column slots of
-// every row and holds its slice of the weight in registers for the whole kernel. h is recomputed
-// from the staged row for the output pass (bit-identical, and it keeps registers low enough for
-// several CTAs per SM); a stage is refilled once every thread is past the next row's barrier.
+// Fast path (rows of H % 8 == 0 elements, 16-byte aligned rows): a persistent, warp-specialised
+// TMA ring. Each CTA owns a contiguous block of rows. Warp 0 is the producer: one lane streams whole
+// rows of x and r into an S-stage shared-memory ring with two bulk copies per row (cp.async.bulk,
+// completion on the stage's `full` mbarrier), refilling a stage as soon as every consumer warp has
+// released it on the stage's `empty` mbarrier. The consumer warps each own the same VPT 16-byte
+// column slots of every row: they wait on `full`, form h = x + r in registers, store round(h) to
+// the residual, reduce sum(h^2) through warp shuffles and one named barrier among consumers, store
+// the normalised row, and release the stage. The weight slice lives in registers for the whole
+// kernel. Every wait is bounded.
 //
 // Generic path (any H, stride or alignment): one CTA per row, two passes over global memory; the
 // second pass recomputes h from the still-unmodified inputs, so no scratch space is needed.
@@ -44,131 +46,149 @@ constexpr int kNormMaxWarps = 32;
 // Shared-memory bytes of the fast path for one CTA.
 __host__ __device__ inline size_t norm_tma_smem_bytes(int H, int stages, int elem_bytes) {
   const size_t stage = 2ull * (size_t)H * (size_t)elem_bytes;
-  return (size_t)stages * stage + (size_t)stages * 8 + 2 * kNormMaxWarps * sizeof(float);
+  return (size_t)stages * stage + (size_t)stages * 16 + 2 * kNormMaxWarps * sizeof(float);
 }
 
+// Named barrier 1 over the consumer warps, OR-reducing a predicate (the producer never joins it).
+__device__ __forceinline__ bool consumers_sync_or(bool pred, int nthreads) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"((uint32_t)pred), "r"(nthreads)
+      : "memory");
+  return out != 0;
+}
+
+constexpr int kNormMaxConsumers = 512;
+
 template <typename T, int VPT, bool QUANT>
-__global__ void __launch_bounds__(512) norm_tma_kernel(const NormArgs a) {
+__global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const NormArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = a.H;
   const int NV = H >> 3;  // 16-byte vectors per row
   const uint32_t row_bytes = (uint32_t)H * (uint32_t)sizeof(T);
   const int S = a.stages;
   unsigned char* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * 2 * row_bytes);
-  float* red = reinterpret_cast<float*>(bars + S);  // [2][kNormMaxWarps]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * 2 * row_bytes);
+  uint64_t* empty = full + S;
+  float* red = reinterpret_cast<float*>(empty + S);  // [2][kNormMaxWarps]
 
   const int tid = threadIdx.x;
-  const int nt = blockDim.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int nwarps = nt >> 5;
+  const int ncons = blockDim.x - 32;  // consumer threads
+  const int ncw = ncons >> 5;
 
   const int64_t row0 = (int64_t)blockIdx.x * a.rows_per_cta;
   const int n = (int)min((int64_t)a.rows_per_cta, a.rows - row0);
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], ncw);
+    }
     fence_barrier_init();
   }
   __syncthreads();
   pdl_wait();
 
-  // This thread's slice of the weight, for every row.
-  Vec16 wv[VPT];
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int v = tid + j * nt;
-    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
-  }
-  float inv_scale = 1.0f;
-  if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
-
   T* const xb = static_cast<T*>(a.x);
   T* const rb = static_cast<T*>(a.r);
-  auto issue = [&](int k) {
-    const int s = k % S;
-    unsigned char* st = ring + (size_t)s * 2 * row_bytes;
-    mbar_arrive_expect_tx(&bars[s], 2 * row_bytes);
-    bulk_load(st, xb + (row0 + k) * a.x_stride, row_bytes, &bars[s]);
-    bulk_load(st + row_bytes, rb + (row0 + k) * a.r_stride, row_bytes, &bars[s]);
-  };
-  if (tid == 0) {
-    const int pre = n < S ? n : S;
-    for (int k = 0; k < pre; ++k) issue(k);
-  }
 
-  const float inv_h = 1.0f / (float)H;
-  int k = 0;
-  for (; k < n; ++k) {
-    const int s = k % S;
-    const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)(k / S) & 1u);
-    const unsigned char* sx = ring + (size_t)s * 2 * row_bytes;
-    const unsigned char* sr = sx + row_bytes;
-    const int64_t row = row0 + k;
-
-    // Pass 1: h = x + r, residual <- round(h), sum of h^2.
-    float ss = 0.f;
-    if (ok) {
-#pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        const int v = tid + j * nt;
-        if (v < NV) {
-          float xf[8], rf[8];
-          unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
-          unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            xf[e] += rf[e];
-            ss += xf[e] * xf[e];
-          }
-          st_plain(rb + row * a.r_stride + (size_t)v * 8, pack8<T>(xf));
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int k = 0; k < n; ++k) {
+        const int s = k % S;
+        if (k >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((k / S) - 1) & 1u)) {
+          atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+          break;
         }
+        unsigned char* st = ring + (size_t)s * 2 * row_bytes;
+        mbar_arrive_expect_tx(&full[s], 2 * row_bytes);
+        bulk_load(st, xb + (row0 + k) * a.x_stride, row_bytes, &full[s]);
+        bulk_load(st + row_bytes, rb + (row0 + k) * a.r_stride, row_bytes, &full[s]);
       }
     }
-    ss = warp_sum(ss);
-    float* red_k = red + (k & 1) * kNormMaxWarps;
-    if (lane == 0) red_k[warp] = ss;
-    // Past this barrier every thread has finished row k-1 entirely, so its stage is free.
-    if (__syncthreads_or(!ok)) break;
-    if (tid == 0 && k >= 1 && k - 1 + S < n) issue(k - 1 + S);
-
-    float tot = 0.f;
-    for (int w = 0; w < nwarps; ++w) tot += red_k[w];
-    const float rstd = rsqrtf(tot * inv_h + a.eps);
-
-    // Pass 2: y = h * rstd * w from the same staged row.
+  } else {
+    const int ct = tid - 32;
+    const int cw = warp - 1;
+    // This thread's slice of the weight, for every row.
+    Vec16 wv[VPT];
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int v = tid + j * nt;
-      if (v < NV) {
-        float xf[8], rf[8], wf[8];
-        unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
-        unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
-        unpack8<T>(wv[j], wf);
+      const int v = ct + j * ncons;
+      if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+    }
+    float inv_scale = 1.0f;
+    if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
+    const float inv_h = 1.0f / (float)H;
+
+    for (int k = 0; k < n; ++k) {
+      const int s = k % S;
+      const bool ok = mbar_wait_bounded(&full[s], (uint32_t)(k / S) & 1u);
+      const unsigned char* sx = ring + (size_t)s * 2 * row_bytes;
+      const unsigned char* sr = sx + row_bytes;
+      const int64_t row = row0 + k;
+
+      // h = x + r (kept in registers), residual <- round(h), sum of h^2.
+      float h[VPT][8];
+      float ss = 0.f;
+      if (ok) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) xf[e] = (xf[e] + rf[e]) * rstd * wf[e];
-        if constexpr (QUANT) {
-          uint2 q;
-          q.x = (uint32_t)f2_to_e4m3x2(xf[0] * inv_scale, xf[1] * inv_scale) |
-                ((uint32_t)f2_to_e4m3x2(xf[2] * inv_scale, xf[3] * inv_scale) << 16);
-          q.y = (uint32_t)f2_to_e4m3x2(xf[4] * inv_scale, xf[5] * inv_scale) |
-                ((uint32_t)f2_to_e4m3x2(xf[6] * inv_scale, xf[7] * inv_scale) << 16);
-          *reinterpret_cast<uint2*>(a.out + row * a.out_stride + (size_t)v * 8) = q;
-        } else {
-          st_plain(xb + row * a.x_stride + (size_t)v * 8, pack8<T>(xf));
+        for (int j = 0; j < VPT; ++j) {
+          const int v = ct + j * ncons;
+          if (v < NV) {
+            float rf[8];
+            unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), h[j]);
+            unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              h[j][e] += rf[e];
+              ss += h[j][e] * h[j][e];
+            }
+            st_plain(rb + row * a.r_stride + (size_t)v * 8, pack8<T>(h[j]));
+          }
+        }
+      }
+      // The staged row is no longer read: hand the stage back to the producer.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+
+      ss = warp_sum(ss);
+      float* red_k = red + (k & 1) * kNormMaxWarps;
+      if (lane == 0) red_k[cw] = ss;
+      if (consumers_sync_or(!ok, ncons)) {
+        if (ct == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+        break;
+      }
+      float tot = 0.f;
+      for (int w = 0; w < ncw; ++w) tot += red_k[w];
+      const float rstd = rsqrtf(tot * inv_h + a.eps);
+
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int v = ct + j * ncons;
+        if (v < NV) {
+          float wf[8];
+          unpack8<T>(wv[j], wf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) h[j][e] = h[j][e] * rstd * wf[e];
+          if constexpr (QUANT) {
+            uint2 q;
+            q.x = (uint32_t)f2_to_e4m3x2(h[j][0] * inv_scale, h[j][1] * inv_scale) |
+                  ((uint32_t)f2_to_e4m3x2(h[j][2] * inv_scale, h[j][3] * inv_scale) << 16);
+            q.y = (uint32_t)f2_to_e4m3x2(h[j][4] * inv_scale, h[j][5] * inv_scale) |
+                  ((uint32_t)f2_to_e4m3x2(h[j][6] * inv_scale, h[j][7] * inv_scale) << 16);
+            *reinterpret_cast<uint2*>(a.out + row * a.out_stride + (size_t)v * 8) = q;
+          } else {
+            st_plain(xb + row * a.x_stride + (size_t)v * 8, pack8<T>(h[j]));
+          }
         }
       }
     }
-  }
-
-  if (k < n && tid == 0) {
-    // A bulk copy never completed: record it, then wait (bounded) for the copies still in flight
-    // into this CTA's ring before the CTA exits and its shared memory is released. Rows issued so
-    // far: [0, min(n, S)) from the prologue and row kk-1+S at every completed iteration kk >= 1.
-    atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
-    const int issued_end = min(n, (k >= 1 ? k - 1 : 0) + S);
-    for (int kk = k; kk < issued_end; ++kk)
-      (void)mbar_wait_bounded(&bars[kk % S], (uint32_t)(kk / S) & 1u);
   }
   pdl_launch_dependents();
 }

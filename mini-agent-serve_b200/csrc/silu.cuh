@@ -3,12 +3,17 @@
 //
 // Semantics follow flashinfer 0.6.11.post2 (FI/data/include/flashinfer/activation.cuh:29-65 with
 // the activation of FI/jit/activation.py:77-80, which uses the __expf intrinsic): fp32 math and
-// one rounding of the product. The quotient here is the IEEE-rounded one.
+// one rounding of the product.
 //
-// Pure streaming (3 x 2 bytes per output element, nothing reused), so the design is about bytes in
-// flight: a 2-D grid of (column tiles, rows), each thread issuing U pairs of 16-byte streaming loads
-// before its first use, with no per-element index division. A scalar path covers d % 8 != 0 and
-// unaligned rows.
+// Pure streaming (6 bytes per output element, nothing reused), so the design is about bytes in
+// flight per SM without spending registers on them. Fast path: a persistent, warp-specialised TMA
+// ring. The work is cut into tiles of (token, kSiluChunk columns); each CTA owns a contiguous range
+// of tiles. Warp 0 is the producer: one lane streams the gate and up halves of each tile into an
+// S-stage shared-memory ring with two bulk copies (cp.async.bulk, completion on the stage's `full`
+// mbarrier). The other warps consume: wait on `full`, read 16-byte vectors from shared memory,
+// compute, store 16-byte vectors to the output, and release the stage on its `empty` mbarrier
+// (one arrival per consumer warp), which the producer waits on before refilling it. Every wait is
+// bounded. A scalar path covers d % 8 != 0 and unaligned rows.
 #pragma once
 
 #include "common.cuh"
@@ -22,43 +27,93 @@ struct SiluArgs {
   int64_t in_stride;   // elements
   int64_t out_stride;  // elements
   int32_t d;
+  int32_t stages;          // TMA ring
+  int64_t tiles_per_cta;   // TMA ring
+  int32_t* fault;
 };
 
 __device__ __forceinline__ float silu_f32(float v) { return v / (1.0f + __expf(-v)); }
 
-constexpr int kSiluThreads = 256;
+constexpr int kSiluThreads = 256;            // scalar path
+constexpr int kSiluConsumerWarps = 8;
+constexpr int kSiluRingThreads = 32 * (1 + kSiluConsumerWarps);
+constexpr int kSiluChunk = 4096;             // columns per tile: 8 KB of gate + 8 KB of up (bf16)
 
-template <typename T, int U>
-__global__ void __launch_bounds__(kSiluThreads) silu_mul_vec_kernel(const SiluArgs a) {
+__host__ __device__ inline size_t silu_ring_smem_bytes(int stages, int elem_bytes) {
+  return (size_t)stages * 2 * kSiluChunk * elem_bytes + (size_t)stages * 16;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const SiluArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int S = a.stages;
+  constexpr int kStageBytes = 2 * kSiluChunk * (int)sizeof(T);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * kStageBytes);
+  uint64_t* empty = full + S;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const int64_t cpr = (a.d + kSiluChunk - 1) / kSiluChunk;  // tiles per row
+  const int64_t total = a.rows * cpr;
+  const int64_t t0 = (int64_t)blockIdx.x * a.tiles_per_cta;
+  const int n = (int)min(a.tiles_per_cta, total - t0);
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kSiluConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
   pdl_wait();
-  const int nvec = a.d >> 3;
-  const int tile = kSiluThreads * U;
-  for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
-    const T* g = static_cast<const T*>(a.in) + row * a.in_stride;
-    const T* u = g + a.d;
-    T* o = static_cast<T*>(a.out) + row * a.out_stride;
-    for (int v0 = blockIdx.x * tile + threadIdx.x; v0 < nvec; v0 += gridDim.x * tile) {
-      Vec16 gv[U], uv[U];
-#pragma unroll
-      for (int i = 0; i < U; ++i) {
-        const int v = v0 + i * kSiluThreads;
-        if (v < nvec) {
-          gv[i] = ld_stream(g + (size_t)v * 8);
-          uv[i] = ld_stream(u + (size_t)v * 8);
+
+  if (warp == 0) {
+    // Producer. A failed wait (which means a copy or a consumer never finished) ends the stream.
+    if (lane == 0) {
+      const T* in = static_cast<const T*>(a.in);
+      for (int k = 0; k < n; ++k) {
+        const int s = k % S;
+        if (k >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((k / S) - 1) & 1u)) {
+          atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+          break;
         }
+        const int64_t tile = t0 + k;
+        const int64_t row = tile / cpr;
+        const int c0 = (int)(tile - row * cpr) * kSiluChunk;
+        const uint32_t bytes = (uint32_t)min(kSiluChunk, a.d - c0) * (uint32_t)sizeof(T);
+        unsigned char* st = smem + (size_t)s * kStageBytes;
+        const T* g = in + row * a.in_stride + c0;
+        mbar_arrive_expect_tx(&full[s], 2 * bytes);
+        bulk_load(st, g, bytes, &full[s]);
+        bulk_load(st + kStageBytes / 2, g + a.d, bytes, &full[s]);
       }
-#pragma unroll
-      for (int i = 0; i < U; ++i) {
-        const int v = v0 + i * kSiluThreads;
-        if (v < nvec) {
-          float gf[8], uf[8], y[8];
-          unpack8<T>(gv[i], gf);
-          unpack8<T>(uv[i], uf);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) y[e] = silu_f32(gf[e]) * uf[e];
-          st_plain(o + (size_t)v * 8, pack8<T>(y));
-        }
+    }
+  } else {
+    const int ct = tid - 32;  // consumer thread index
+    T* out = static_cast<T*>(a.out);
+    for (int k = 0; k < n; ++k) {
+      const int s = k % S;
+      if (!mbar_wait_bounded(&full[s], (uint32_t)(k / S) & 1u)) {
+        if (lane == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+        break;
       }
+      const int64_t tile = t0 + k;
+      const int64_t row = tile / cpr;
+      const int c0 = (int)(tile - row * cpr) * kSiluChunk;
+      const int nv = min(kSiluChunk, a.d - c0) >> 3;
+      const unsigned char* sg = smem + (size_t)s * kStageBytes;
+      const unsigned char* su = sg + kStageBytes / 2;
+      T* o = out + row * a.out_stride + c0;
+      for (int v = ct; v < nv; v += 32 * kSiluConsumerWarps) {
+        float gf[8], uf[8], y[8];
+        unpack8<T>(*reinterpret_cast<const Vec16*>(sg + (size_t)v * 16), gf);
+        unpack8<T>(*reinterpret_cast<const Vec16*>(su + (size_t)v * 16), uf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = silu_f32(gf[e]) * uf[e];
+        st_plain(o + (size_t)v * 8, pack8<T>(y));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
   }
   pdl_launch_dependents();

@@ -1,0 +1,159 @@
+// torch_ops.cpp -- the `mas_b200::*` PyTorch operators, implemented in C++ over the C ABI.
+//
+// Each operator unpacks its tensors into the plain pointers, sizes and strides of the matching
+// include/mas_b200.h entry point and launches on the tensor's device and current stream. Doing this in
+// C++ keeps a call at dispatcher cost (a few microseconds): the serving loop issues several of these
+// ops per layer, and a Python-level operator body would make short steps CPU-bound. The fake (meta)
+// kernels that torch.compile traces with are registered from Python (ops.py); the argument checks
+// that must raise flashinfer's Python exception types stay in the Python wrappers, and the checks
+// here are the last line (TORCH_CHECK -> RuntimeError).
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <optional>
+
+#include "../../include/mas_b200.h"
+
+namespace {
+
+int act_code(const at::Tensor& t) {
+  if (t.scalar_type() == at::kBFloat16) return MAS_DTYPE_BF16;
+  if (t.scalar_type() == at::kHalf) return MAS_DTYPE_FP16;
+  TORCH_CHECK(false, "mas_b200: unsupported dtype ", t.scalar_type(), "; expected bfloat16 or float16");
+}
+
+int id_code(const at::Tensor& t) {
+  if (t.scalar_type() == at::kInt) return MAS_DTYPE_INT32;
+  if (t.scalar_type() == at::kLong) return MAS_DTYPE_INT64;
+  TORCH_CHECK(false, "mas_b200: indices must be int32 or int64, got ", t.scalar_type());
+}
+
+void check(int rc, const char* fn) {
+  TORCH_CHECK(rc == MAS_OK, fn, " failed with status ", rc, ": ", mas_status_string(rc));
+}
+
+// [rows, cols] view of a tensor whose last dimension is contiguous and whose leading dimensions
+// collapse into one: returns (rows, row stride in elements).
+struct Rows {
+  int64_t rows;
+  int64_t cols;
+  int64_t stride;
+};
+
+Rows rows_of(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.dim() >= 1, "mas_b200: ", name, " must have at least one dimension");
+  const int64_t cols = t.size(-1);
+  TORCH_CHECK(t.stride(-1) == 1 || cols <= 1, "mas_b200: ", name, " must be contiguous in its last dimension");
+  if (t.dim() == 1) return {1, cols, cols};
+  int64_t rows = 1;
+  for (int64_t d = 0; d < t.dim() - 1; ++d) rows *= t.size(d);
+  const int64_t stride = t.stride(-2);
+  for (int64_t d = 0; d + 2 < t.dim(); ++d) {
+    TORCH_CHECK(t.size(d + 1) == 1 || t.stride(d) == t.stride(d + 1) * t.size(d + 1),
+                "mas_b200: ", name, "'s leading dimensions must be collapsible into one");
+  }
+  return {rows, cols, rows > 1 ? stride : cols};
+}
+
+void* stream_of(const at::Tensor& t) {
+  return static_cast<void*>(c10::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+void fused_add_rmsnorm(at::Tensor input, at::Tensor residual, at::Tensor weight, double eps, bool enable_pdl) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  const Rows x = rows_of(input, "input"), r = rows_of(residual, "residual");
+  TORCH_CHECK(x.rows == r.rows && x.cols == r.cols, "mas_b200: input and residual shapes differ");
+  check(mas_fused_add_rmsnorm(input.data_ptr(), residual.data_ptr(), weight.data_ptr(), x.rows, x.cols, x.stride,
+                              r.stride, static_cast<float>(eps), act_code(input), enable_pdl, stream_of(input)),
+        "mas_fused_add_rmsnorm");
+}
+
+void fused_add_rmsnorm_quant(at::Tensor out, at::Tensor input, at::Tensor residual, at::Tensor weight,
+                             at::Tensor scale, double eps, bool enable_pdl) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  const Rows o = rows_of(out, "out"), x = rows_of(input, "input"), r = rows_of(residual, "residual");
+  TORCH_CHECK(o.rows == x.rows && x.rows == r.rows && o.cols == x.cols && x.cols == r.cols,
+              "mas_b200: out, input and residual shapes differ");
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn, "mas_b200: out must be float8_e4m3fn");
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.numel() == 1, "mas_b200: scale must be one fp32 value");
+  check(mas_fused_add_rmsnorm_quant(out.data_ptr(), input.data_ptr(), residual.data_ptr(), weight.data_ptr(),
+                                    scale.data_ptr<float>(), x.rows, x.cols, o.stride, x.stride, r.stride,
+                                    static_cast<float>(eps), act_code(input), MAS_DTYPE_FP8_E4M3, enable_pdl,
+                                    stream_of(input)),
+        "mas_fused_add_rmsnorm_quant");
+}
+
+void silu_and_mul(at::Tensor out, at::Tensor input, bool enable_pdl) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  const Rows o = rows_of(out, "out"), x = rows_of(input, "input");
+  TORCH_CHECK(o.rows == x.rows && x.cols == 2 * o.cols, "mas_b200: out must be input[..., :d]-shaped");
+  check(mas_silu_and_mul(out.data_ptr(), input.data_ptr(), x.rows, o.cols, o.stride, x.stride, act_code(input),
+                         enable_pdl, stream_of(input)),
+        "mas_silu_and_mul");
+}
+
+void apply_rope_pos_ids_cos_sin_cache(at::Tensor q, at::Tensor k, at::Tensor cos_sin_cache, at::Tensor pos_ids,
+                                      bool interleave, bool enable_pdl, std::optional<at::Tensor> status) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3, "mas_b200: q and k must be (tokens, heads, head_size) views");
+  TORCH_CHECK(cos_sin_cache.dim() == 2 && cos_sin_cache.is_contiguous(), "mas_b200: cos_sin_cache must be contiguous");
+  TORCH_CHECK(q.size(2) == k.size(2), "mas_b200: q and k head sizes differ");
+  int32_t* st = status.has_value() ? status->data_ptr<int32_t>() : nullptr;
+  check(mas_rope_cos_sin_cache_inplace(pos_ids.data_ptr(), id_code(pos_ids), q.data_ptr(), k.data_ptr(),
+                                       cos_sin_cache.data_ptr<float>(), q.size(0), q.size(1), k.size(1), q.size(2),
+                                       cos_sin_cache.size(1), cos_sin_cache.size(0), q.stride(0), q.stride(1),
+                                       k.stride(0), k.stride(1), interleave ? 0 : 1, act_code(q), st, enable_pdl,
+                                       stream_of(q)),
+        "mas_rope_cos_sin_cache_inplace");
+}
+
+void gather(at::Tensor& out, const at::Tensor& ids, const at::Tensor& weight, bool enable_pdl,
+            const std::optional<at::Tensor>& status) {
+  TORCH_CHECK(weight.dim() == 2 && weight.stride(1) == 1, "mas_b200: weight must be (num_embeddings, dim)");
+  TORCH_CHECK(ids.is_contiguous(), "mas_b200: input_ids must be contiguous");
+  TORCH_CHECK(out.is_contiguous(), "mas_b200: out must be contiguous");
+  int32_t* st = status.has_value() ? status->data_ptr<int32_t>() : nullptr;
+  check(mas_embedding_gather(out.data_ptr(), weight.data_ptr(), ids.data_ptr(), id_code(ids), ids.numel(),
+                             weight.size(1), weight.size(0), weight.size(1), weight.stride(0),
+                             static_cast<int>(weight.element_size()), st, enable_pdl, stream_of(weight)),
+        "mas_embedding_gather");
+}
+
+at::Tensor embedding(at::Tensor input_ids, at::Tensor weight, bool enable_pdl, std::optional<at::Tensor> status) {
+  const c10::cuda::CUDAGuard guard(weight.device());
+  std::vector<int64_t> shape(input_ids.sizes().begin(), input_ids.sizes().end());
+  shape.push_back(weight.size(1));
+  at::Tensor out = at::empty(shape, weight.options());
+  gather(out, input_ids.contiguous(), weight, enable_pdl, status);
+  return out;
+}
+
+void embedding_out(at::Tensor out, at::Tensor input_ids, at::Tensor weight, bool enable_pdl,
+                   std::optional<at::Tensor> status) {
+  const c10::cuda::CUDAGuard guard(weight.device());
+  gather(out, input_ids, weight, enable_pdl, status);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(mas_b200, m) {
+  m.def("fused_add_rmsnorm(Tensor(a!) input, Tensor(b!) residual, Tensor weight, float eps, bool enable_pdl) -> ()");
+  m.def("fused_add_rmsnorm_quant(Tensor(a!) out, Tensor input, Tensor(b!) residual, Tensor weight, Tensor scale, "
+        "float eps, bool enable_pdl) -> ()");
+  m.def("silu_and_mul(Tensor(a!) out, Tensor input, bool enable_pdl) -> ()");
+  m.def("apply_rope_pos_ids_cos_sin_cache(Tensor(a!) q, Tensor(b!) k, Tensor cos_sin_cache, Tensor pos_ids, "
+        "bool interleave, bool enable_pdl, Tensor(c!)? status) -> ()");
+  m.def("embedding(Tensor input_ids, Tensor weight, bool enable_pdl, Tensor(a!)? status) -> Tensor");
+  m.def("embedding_out(Tensor(a!) out, Tensor input_ids, Tensor weight, bool enable_pdl, Tensor(b!)? status) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(mas_b200, CUDA, m) {
+  m.impl("fused_add_rmsnorm", &fused_add_rmsnorm);
+  m.impl("fused_add_rmsnorm_quant", &fused_add_rmsnorm_quant);
+  m.impl("silu_and_mul", &silu_and_mul);
+  m.impl("apply_rope_pos_ids_cos_sin_cache", &apply_rope_pos_ids_cos_sin_cache);
+  m.impl("embedding", &embedding);
+  m.impl("embedding_out", &embedding_out);
+}

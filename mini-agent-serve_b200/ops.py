@@ -12,11 +12,13 @@ flashinfer 0.6.11.post2 functions that miniagentserve/models/devstral2/devstral2
 plus the token-embedding gather behind nn.Embedding (devstral2.py:260, :282), as `embedding` and the
 `Embedding` module (embedding.py).
 
-Each function is a thin Python check layer over a `torch.library` custom op in the `mas_b200`
-namespace (opaque to torch.compile through its fake kernel, mirroring flashinfer's
-register_custom_op/register_fake_op, FI/activation.py:48-58), whose CUDA implementation calls the
-C ABI of libmas_b200.so (include/mas_b200.h) on the current stream. There is no CPU
-implementation: the ops are registered for CUDA only, and the library must be present.
+Each function is a thin Python check layer (raising flashinfer's exception types) over a
+`mas_b200::*` torch operator. The operators are defined and implemented in C++
+(csrc/torch_ops.cpp, loaded by _lib) over the C ABI of libmas_b200.so (include/mas_b200.h) and launch
+on the current stream; their fake kernels, registered here, make them opaque nodes under
+torch.compile (mirroring flashinfer's register_custom_op/register_fake_op, FI/activation.py:48-58).
+There is no CPU implementation: the operators are registered for CUDA only, and the libraries must
+be present.
 """
 from __future__ import annotations
 
@@ -44,49 +46,11 @@ _ACT_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_FP16}
 _ID_DTYPES = {torch.int32: _lib.DTYPE_INT32, torch.int64: _lib.DTYPE_INT64}
 
 
-def _stream(t: torch.Tensor) -> int:
-    return torch.cuda.current_stream(t.device).cuda_stream
-
-
 def _act_code(t: torch.Tensor) -> int:
     try:
         return _ACT_DTYPES[t.dtype]
     except KeyError:
         raise ValueError(f"unsupported dtype {t.dtype}; expected bfloat16 or float16") from None
-
-
-def _rows(t: torch.Tensor, name: str) -> torch.Tensor:
-    """`t` as a 2-D [tokens, hidden] view (hidden contiguous), without copying."""
-    if t.dim() == 0:
-        raise ValueError(f"{name} must have at least one dimension")
-    if t.stride(-1) != 1 and t.shape[-1] > 1:
-        raise ValueError(f"{name} must be contiguous in its last dimension")
-    if t.dim() == 1:
-        return t.view(1, -1)
-    try:
-        return t.view(-1, t.shape[-1])
-    except RuntimeError:
-        raise ValueError(f"{name}'s leading dimensions must be collapsible into one") from None
-
-
-class _DeviceGuard:
-    """Makes `t`'s device current for the C ABI (which launches on the current device)."""
-
-    __slots__ = ("dev", "prev")
-
-    def __init__(self, t: torch.Tensor):
-        self.dev = t.device.index
-        self.prev = None
-
-    def __enter__(self):
-        cur = torch.cuda.current_device()
-        if self.dev is not None and cur != self.dev:
-            self.prev = cur
-            torch.cuda.set_device(self.dev)
-
-    def __exit__(self, *exc):
-        if self.prev is not None:
-            torch.cuda.set_device(self.prev)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -123,28 +87,29 @@ def read_status(device: Union[int, torch.device, None] = None, clear: bool = Tru
     return v
 
 
-def _status_ptr(t: torch.Tensor) -> Optional[int]:
-    w = status_word(t.device)
-    return None if w is None else w.data_ptr()
+def _status_arg(device: torch.device) -> Optional[torch.Tensor]:
+    """The status word to hand a kernel: none off CUDA, and none while torch.compile traces (the
+    word is a side channel for eager and graph-replayed steps, not part of the traced program)."""
+    if device.type != "cuda" or torch.compiler.is_compiling():
+        return None
+    w = _status.get(device.index)
+    return w if w is not None else status_word(device)
 
 
 # ------------------------------------------------------------------------------------------------
 # Fused add RMSNorm.
 # ------------------------------------------------------------------------------------------------
-@torch.library.custom_op("mas_b200::fused_add_rmsnorm", mutates_args=("input", "residual"), device_types="cuda")
-def _fused_add_rmsnorm_op(input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float,
-                          enable_pdl: bool) -> None:
-    x, r = _rows(input, "input"), _rows(residual, "residual")
-    with _DeviceGuard(x):
-        rc = _lib.lib.mas_fused_add_rmsnorm(
-            x.data_ptr(), r.data_ptr(), weight.data_ptr(), x.shape[0], x.shape[1], x.stride(0), r.stride(0),
-            float(eps), _act_code(x), int(enable_pdl), _stream(x))
-    _lib.check("mas_fused_add_rmsnorm", rc)
-
-
-@_fused_add_rmsnorm_op.register_fake
+@torch.library.register_fake("mas_b200::fused_add_rmsnorm")
 def _(input, residual, weight, eps, enable_pdl) -> None:
     return None
+
+
+_OP_NORM = torch.ops.mas_b200.fused_add_rmsnorm.default
+_OP_NORM_QUANT = torch.ops.mas_b200.fused_add_rmsnorm_quant.default
+_OP_SILU = torch.ops.mas_b200.silu_and_mul.default
+_OP_ROPE = torch.ops.mas_b200.apply_rope_pos_ids_cos_sin_cache.default
+_OP_EMBED = torch.ops.mas_b200.embedding.default
+_OP_EMBED_OUT = torch.ops.mas_b200.embedding_out.default
 
 
 def _check_norm(input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor) -> None:
@@ -166,8 +131,7 @@ def fused_add_rmsnorm(input: torch.Tensor, residual: torch.Tensor, weight: torch
     Same signature and meaning as flashinfer.norm.fused_add_rmsnorm (FI/norm/__init__.py:236-274).
     """
     _check_norm(input, residual, weight)
-    pdl = True if enable_pdl is None else bool(enable_pdl)
-    torch.ops.mas_b200.fused_add_rmsnorm(input, residual, weight, float(eps), pdl)
+    _OP_NORM(input, residual, weight, float(eps), True if enable_pdl is None else bool(enable_pdl))
 
 
 def _normalize_scale(scale: Union[float, torch.Tensor], ref: torch.Tensor) -> torch.Tensor:
@@ -187,19 +151,7 @@ def _normalize_scale(scale: Union[float, torch.Tensor], ref: torch.Tensor) -> to
     return scale.contiguous()
 
 
-@torch.library.custom_op("mas_b200::fused_add_rmsnorm_quant", mutates_args=("out", "residual"), device_types="cuda")
-def _fused_add_rmsnorm_quant_op(out: torch.Tensor, input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
-                                scale: torch.Tensor, eps: float, enable_pdl: bool) -> None:
-    o, x, r = _rows(out, "out"), _rows(input, "input"), _rows(residual, "residual")
-    with _DeviceGuard(x):
-        rc = _lib.lib.mas_fused_add_rmsnorm_quant(
-            o.data_ptr(), x.data_ptr(), r.data_ptr(), weight.data_ptr(), scale.data_ptr(), x.shape[0], x.shape[1],
-            o.stride(0), x.stride(0), r.stride(0), float(eps), _act_code(x), _lib.DTYPE_FP8_E4M3, int(enable_pdl),
-            _stream(x))
-    _lib.check("mas_fused_add_rmsnorm_quant", rc)
-
-
-@_fused_add_rmsnorm_quant_op.register_fake
+@torch.library.register_fake("mas_b200::fused_add_rmsnorm_quant")
 def _(out, input, residual, weight, scale, eps, enable_pdl) -> None:
     return None
 
@@ -219,23 +171,13 @@ def fused_add_rmsnorm_quant(out: torch.Tensor, input: torch.Tensor, residual: to
     if out.shape != input.shape:
         raise ValueError(f"out {tuple(out.shape)} and input {tuple(input.shape)} differ")
     scale = _normalize_scale(scale, input)
-    pdl = True if enable_pdl is None else bool(enable_pdl)
-    torch.ops.mas_b200.fused_add_rmsnorm_quant(out, input, residual, weight, scale, float(eps), pdl)
+    _OP_NORM_QUANT(out, input, residual, weight, scale, float(eps), True if enable_pdl is None else bool(enable_pdl))
 
 
 # ------------------------------------------------------------------------------------------------
 # SiLU and mul.
 # ------------------------------------------------------------------------------------------------
-@torch.library.custom_op("mas_b200::silu_and_mul", mutates_args=("out",), device_types="cuda")
-def _silu_and_mul_op(out: torch.Tensor, input: torch.Tensor, enable_pdl: bool) -> None:
-    o, x = _rows(out, "out"), _rows(input, "input")
-    with _DeviceGuard(x):
-        rc = _lib.lib.mas_silu_and_mul(o.data_ptr(), x.data_ptr(), x.shape[0], o.shape[1], o.stride(0), x.stride(0),
-                                       _act_code(x), int(enable_pdl), _stream(x))
-    _lib.check("mas_silu_and_mul", rc)
-
-
-@_silu_and_mul_op.register_fake
+@torch.library.register_fake("mas_b200::silu_and_mul")
 def _(out, input, enable_pdl) -> None:
     return None
 
@@ -264,30 +206,15 @@ def silu_and_mul(input: torch.Tensor, out: Optional[torch.Tensor] = None,
     else:
         out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), device=input.device, dtype=input.dtype)
     _act_code(input)
-    pdl = True if enable_pdl is None else bool(enable_pdl)
-    torch.ops.mas_b200.silu_and_mul(out, input, pdl)
+    _OP_SILU(out, input, True if enable_pdl is None else bool(enable_pdl))
     return out
 
 
 # ------------------------------------------------------------------------------------------------
 # Rotary embedding from the fp32 cos|sin cache.
 # ------------------------------------------------------------------------------------------------
-@torch.library.custom_op("mas_b200::apply_rope_pos_ids_cos_sin_cache", mutates_args=("q", "k"),
-                         device_types="cuda")
-def _rope_op(q: torch.Tensor, k: torch.Tensor, cos_sin_cache: torch.Tensor, pos_ids: torch.Tensor,
-             interleave: bool, enable_pdl: bool) -> None:
-    with _DeviceGuard(q):
-        status = _status_ptr(q)
-        rc = _lib.lib.mas_rope_cos_sin_cache_inplace(
-            pos_ids.data_ptr(), _ID_DTYPES[pos_ids.dtype], q.data_ptr(), k.data_ptr(), cos_sin_cache.data_ptr(),
-            q.shape[0], q.shape[1], k.shape[1], q.shape[2], cos_sin_cache.shape[1], cos_sin_cache.shape[0],
-            q.stride(0), q.stride(1), k.stride(0), k.stride(1), int(not interleave), _act_code(q), status,
-            int(enable_pdl), _stream(q))
-    _lib.check("mas_rope_cos_sin_cache_inplace", rc)
-
-
-@_rope_op.register_fake
-def _(q, k, cos_sin_cache, pos_ids, interleave, enable_pdl) -> None:
+@torch.library.register_fake("mas_b200::apply_rope_pos_ids_cos_sin_cache")
+def _(q, k, cos_sin_cache, pos_ids, interleave, enable_pdl, status) -> None:
     return None
 
 
@@ -320,43 +247,20 @@ def apply_rope_with_cos_sin_cache_inplace(positions: torch.Tensor, query: torch.
         return
     q = query.view(query.shape[0], -1, head_size)
     k = key.view(key.shape[0], -1, head_size)
-    pdl = True if enable_pdl is None else bool(enable_pdl)
-    torch.ops.mas_b200.apply_rope_pos_ids_cos_sin_cache(q, k, cos_sin_cache, positions, not is_neox, pdl)
+    _OP_ROPE(q, k, cos_sin_cache, positions, not is_neox, True if enable_pdl is None else bool(enable_pdl),
+             _status_arg(query.device))
 
 
 # ------------------------------------------------------------------------------------------------
 # Token-embedding gather.
 # ------------------------------------------------------------------------------------------------
-def _gather(out: torch.Tensor, ids: torch.Tensor, weight: torch.Tensor, enable_pdl: bool) -> None:
-    o = out.view(-1, weight.shape[1])
-    i = ids.reshape(-1)
-    with _DeviceGuard(weight):
-        rc = _lib.lib.mas_embedding_gather(
-            o.data_ptr(), weight.data_ptr(), i.data_ptr(), _ID_DTYPES[i.dtype], i.shape[0], weight.shape[1],
-            weight.shape[0], o.stride(0), weight.stride(0), weight.element_size(), _status_ptr(weight),
-            int(enable_pdl), _stream(weight))
-    _lib.check("mas_embedding_gather", rc)
-
-
-@torch.library.custom_op("mas_b200::embedding", mutates_args=(), device_types="cuda")
-def _embedding_op(input_ids: torch.Tensor, weight: torch.Tensor, enable_pdl: bool) -> torch.Tensor:
-    out = torch.empty(tuple(input_ids.shape) + (weight.shape[1],), dtype=weight.dtype, device=weight.device)
-    _gather(out, input_ids, weight, enable_pdl)
-    return out
-
-
-@_embedding_op.register_fake
-def _(input_ids, weight, enable_pdl):
+@torch.library.register_fake("mas_b200::embedding")
+def _(input_ids, weight, enable_pdl, status):
     return weight.new_empty(tuple(input_ids.shape) + (weight.shape[1],))
 
 
-@torch.library.custom_op("mas_b200::embedding_out", mutates_args=("out",), device_types="cuda")
-def _embedding_out_op(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tensor, enable_pdl: bool) -> None:
-    _gather(out, input_ids, weight, enable_pdl)
-
-
-@_embedding_out_op.register_fake
-def _(out, input_ids, weight, enable_pdl) -> None:
+@torch.library.register_fake("mas_b200::embedding_out")
+def _(out, input_ids, weight, enable_pdl, status) -> None:
     return None
 
 
@@ -374,8 +278,7 @@ def embedding(input_ids: torch.Tensor, weight: torch.Tensor, enable_pdl: Optiona
     in the device status word (`read_status`), where aten would raise a device-side assert.
     """
     _check_embedding(input_ids, weight)
-    pdl = True if enable_pdl is None else bool(enable_pdl)
-    return torch.ops.mas_b200.embedding(input_ids, weight, pdl)
+    return _OP_EMBED(input_ids, weight, True if enable_pdl is None else bool(enable_pdl), _status_arg(weight.device))
 
 
 def embedding_out(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tensor,
@@ -386,6 +289,6 @@ def embedding_out(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tens
         raise ValueError("out must be (*input_ids.shape, embedding_dim) with weight's dtype")
     if not out.is_contiguous():
         raise ValueError("out must be contiguous")
-    pdl = True if enable_pdl is None else bool(enable_pdl)
-    torch.ops.mas_b200.embedding_out(out, input_ids, weight, pdl)
+    _OP_EMBED_OUT(out, input_ids.contiguous(), weight, True if enable_pdl is None else bool(enable_pdl),
+                  _status_arg(weight.device))
     return out

@@ -87,9 +87,9 @@ def test_ops_registered_with_mutation_annotations():
         "fused_add_rmsnorm": ("input", "residual"),
         "fused_add_rmsnorm_quant": ("out", "residual"),
         "silu_and_mul": ("out",),
-        "apply_rope_pos_ids_cos_sin_cache": ("q", "k"),
-        "embedding_out": ("out",),
-        "embedding": (),
+        "apply_rope_pos_ids_cos_sin_cache": ("q", "k", "status"),
+        "embedding_out": ("out", "status"),
+        "embedding": ("status",),
     }
     for name, mutated in expect.items():
         schema = getattr(torch.ops.mas_b200, name).default._schema
