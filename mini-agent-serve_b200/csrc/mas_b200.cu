@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -24,7 +25,8 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 constexpr size_t kMaxSmemPerCta = 227 * 1024;
-constexpr size_t kRingBytesPerSm = 192 * 1024;  // shared memory the TMA rings may use per SM
+// Shared memory the TMA rings may use per SM: the SM has 228 KB, less 1 KB reserved per resident CTA.
+constexpr size_t kRingBytesPerSm = 216 * 1024;
 
 struct DeviceState {
   std::once_flag once;
@@ -39,6 +41,12 @@ int env_int(const char* name, int fallback) {
   const char* v = std::getenv(name);
   if (v == nullptr || *v == '\0') return fallback;
   return std::atoi(v);
+}
+
+// Optional choice between two fast-path designs of a kernel ("ring" or another name), read once.
+bool env_is(const char* name, const char* value) {
+  const char* v = std::getenv(name);
+  return v != nullptr && std::strcmp(v, value) == 0;
 }
 
 template <typename K>
@@ -66,8 +74,20 @@ cudaError_t prepare_current(DeviceState& st, int device) {
   if ((e = opt_in_norm<__nv_bfloat16, true>()) != cudaSuccess) return e;
   if ((e = opt_in_norm<__half, false>()) != cudaSuccess) return e;
   if ((e = opt_in_norm<__half, true>()) != cudaSuccess) return e;
+  if ((e = opt_in_smem(norm_row_kernel<__nv_bfloat16, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(norm_row_kernel<__nv_bfloat16, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(norm_row_kernel<__half, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(norm_row_kernel<__half, true>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__half>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int32_t, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int32_t, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int64_t, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int64_t, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<__half, int32_t, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<__half, int32_t, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<__half, int64_t, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<__half, int64_t, false>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(embed_tma_kernel<int32_t>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(embed_tma_kernel<int64_t>)) != cudaSuccess) return e;
   void* fault = nullptr;
@@ -194,6 +214,24 @@ int launch_norm_tma(NormArgs a, int vpt, int nt, size_t smem, int grid, void* st
 template <typename T, bool Q>
 int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int pdl) {
   const int H = a.H;
+  static const bool use_ring = env_is("MAS_NORM_IMPL", "ring");
+  if (fast_ok && H % 8 == 0 && !use_ring) {
+    // Row-block CTAs: threads per row grow with H (32 ... 256), 128 or 256 threads per CTA.
+    static const int env_tpr = env_int("MAS_NORM_TPR", 0);
+    static const int env_cta = env_int("MAS_NORM_CTA_THREADS", 0);
+    int tpr = H <= 3072 ? 32 : H <= 6144 ? 64 : H <= 16384 ? 128 : 256;
+    if (env_tpr > 0) tpr = env_tpr;
+    int cta = env_cta > 0 ? env_cta : std::max(128, tpr);
+    tpr = std::max(32, std::min(tpr, kNormRowMaxThreads)) / 32 * 32;
+    cta = std::max(tpr, std::min(cta, kNormRowMaxThreads)) / tpr * tpr;
+    const int rpc = cta / tpr;
+    const size_t smem = norm_row_smem_bytes(H, rpc, (int)sizeof(T));
+    if (smem <= kMaxSmemPerCta) {
+      const int64_t grid = ceil_div(a.rows, rpc);
+      if (grid <= INT32_MAX)
+        return launch(norm_row_kernel<T, Q>, dim3((unsigned)grid), dim3(cta), smem, stream, pdl, a, tpr, rpc);
+    }
+  }
   if (fast_ok && H % 8 == 0) {
     const int nv = H / 8;
     const int vpt = (int)ceil_div(nv, kNormMaxConsumers);
@@ -329,9 +367,17 @@ int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
   SiluArgs a = {};
   a.out = out; a.in = input; a.rows = num_tokens; a.in_stride = input_stride;
   a.out_stride = out_stride; a.d = (int32_t)d; a.fault = st->fault;
-  const bool ring = d % 8 == 0 && aligned(out, 16) && aligned(input, 16) && input_stride % 8 == 0 &&
-                    out_stride % 8 == 0;
-  if (ring) {
+  const bool vec = d % 8 == 0 && aligned(out, 16) && aligned(input, 16) && input_stride % 8 == 0 &&
+                   out_stride % 8 == 0;
+  static const bool use_vec = env_is("MAS_SILU_IMPL", "vec");
+  if (vec && use_vec) {
+    const unsigned gx = (unsigned)ceil_div(d / 8, kSiluThreads);
+    const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, 65535);
+    if (dtype == MAS_DTYPE_BF16)
+      return launch(silu_mul_vec_kernel<__nv_bfloat16>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+    return launch(silu_mul_vec_kernel<__half>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+  }
+  if (vec) {
     static const int env_stages = env_int("MAS_SILU_STAGES", 0);
     static const int env_ctas = env_int("MAS_SILU_CTAS_PER_SM", 0);
     const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 6));
@@ -406,6 +452,50 @@ int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, v
     return neox ? launch(KERNEL<__half, int32_t, true>, GRID, blk, 0, stream, enable_pdl, a)        \
                 : launch(KERNEL<__half, int32_t, false>, GRID, blk, 0, stream, enable_pdl, a);      \
   } while (0)
+  // Token-staged TMA ring: q heads and k heads contiguous within each token, 16-byte aligned rows.
+  static const bool force_vec = env_is("MAS_ROPE_IMPL", "vec");
+  const bool ring = vec && !force_vec && head_size % 8 == 0 &&
+                    (num_q_heads == 0 || q_stride_head == head_size) &&
+                    (num_kv_heads == 0 || k_stride_head == head_size);
+  if (ring) {
+    RopeRingArgs r = {};
+    r.pos = positions; r.q = query; r.k = key; r.cache = cos_sin_cache; r.T = num_tokens; r.P = max_positions;
+    r.qsn = q_stride_token; r.ksn = k_stride_token; r.Hq = (int32_t)num_q_heads; r.Hkv = (int32_t)num_kv_heads;
+    r.D = (int32_t)head_size; r.rd = (int32_t)rotary_dim; r.status = status; r.fault = st->fault;
+    const uint32_t stage = rope_stage_bytes(r.Hq, r.Hkv, r.D, r.rd, 2);
+    static const int env_stages = env_int("MAS_ROPE_STAGES", 0);
+    const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
+    const size_t per_cta = rope_ring_smem_bytes(stage, stages, kRopeMaxTokensPerCta);
+    if (per_cta <= kMaxSmemPerCta) {
+      const void* fn = bf ? (i64 ? (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, true>
+                                         : (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, false>)
+                                 : (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int32_t, true>
+                                         : (const void*)rope_ring_kernel<__nv_bfloat16, int32_t, false>))
+                          : (i64 ? (neox ? (const void*)rope_ring_kernel<__half, int64_t, true>
+                                         : (const void*)rope_ring_kernel<__half, int64_t, false>)
+                                 : (neox ? (const void*)rope_ring_kernel<__half, int32_t, true>
+                                         : (const void*)rope_ring_kernel<__half, int32_t, false>));
+      int ctas = (int)std::max<size_t>(1, kRingBytesPerSm / per_cta);
+      ctas = std::min(ctas, resident_ctas(fn, kRopeRingThreads, per_cta));
+      int64_t grid = std::max<int64_t>((int64_t)st->sm_count * ctas, ceil_div(num_tokens, kRopeMaxTokensPerCta));
+      grid = std::min<int64_t>(grid, num_tokens);
+      r.tokens_per_cta = (int32_t)ceil_div(num_tokens, grid);
+      grid = ceil_div(num_tokens, r.tokens_per_cta);
+      r.stages = stages;
+      const size_t smem = rope_ring_smem_bytes(stage, stages, r.tokens_per_cta);
+      const dim3 g((unsigned)grid), b(kRopeRingThreads);
+      if (bf) {
+        if (i64) return neox ? launch(rope_ring_kernel<__nv_bfloat16, int64_t, true>, g, b, smem, stream, enable_pdl, r)
+                             : launch(rope_ring_kernel<__nv_bfloat16, int64_t, false>, g, b, smem, stream, enable_pdl, r);
+        return neox ? launch(rope_ring_kernel<__nv_bfloat16, int32_t, true>, g, b, smem, stream, enable_pdl, r)
+                    : launch(rope_ring_kernel<__nv_bfloat16, int32_t, false>, g, b, smem, stream, enable_pdl, r);
+      }
+      if (i64) return neox ? launch(rope_ring_kernel<__half, int64_t, true>, g, b, smem, stream, enable_pdl, r)
+                           : launch(rope_ring_kernel<__half, int64_t, false>, g, b, smem, stream, enable_pdl, r);
+      return neox ? launch(rope_ring_kernel<__half, int32_t, true>, g, b, smem, stream, enable_pdl, r)
+                  : launch(rope_ring_kernel<__half, int32_t, false>, g, b, smem, stream, enable_pdl, r);
+    }
+  }
   if (vec) {
     a.tpu = (int32_t)(rotary_dim / 16);
     const int64_t upb = kRopeThreads / a.tpu;

@@ -193,6 +193,104 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
   pdl_launch_dependents();
 }
 
+// Row-block variant of the fast path: a non-persistent grid of small CTAs, each owning `rpc` rows
+// handled by `tpr` threads apiece. Thread 0 stages all of the CTA's x and r rows with bulk copies
+// on one mbarrier; each row's threads then form h from shared memory, reduce it (warp shuffles, a
+// shared partial sum per warp, one CTA barrier) and write both outputs, re-reading h from shared
+// memory for the second pass. Several such CTAs per SM keep several rows in their reduction phase
+// at once. The wait is bounded.
+constexpr int kNormRowMaxThreads = 512;
+
+__host__ __device__ inline size_t norm_row_smem_bytes(int H, int rpc, int elem_bytes) {
+  return (size_t)rpc * 2 * (size_t)H * (size_t)elem_bytes + 16 + (size_t)(kNormRowMaxThreads / 32) * sizeof(float);
+}
+
+template <typename T, bool QUANT>
+__global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const NormArgs a, int tpr, int rpc) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int H = a.H;
+  const int NV = H >> 3;
+  const uint32_t row_bytes = (uint32_t)H * (uint32_t)sizeof(T);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + (size_t)rpc * 2 * row_bytes);
+  float* red = reinterpret_cast<float*>(bar + 2);
+  const int tid = threadIdx.x;
+  const int rr = tid / tpr;   // row slot of this thread within the CTA
+  const int rt = tid - rr * tpr;
+  const int64_t row0 = (int64_t)blockIdx.x * rpc;
+  const int nrows = (int)min((int64_t)rpc, a.rows - row0);
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  T* const xb = static_cast<T*>(a.x);
+  T* const rb = static_cast<T*>(a.r);
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar, (uint32_t)nrows * 2 * row_bytes);
+    for (int i = 0; i < nrows; ++i) {
+      unsigned char* st = smem + (size_t)i * 2 * row_bytes;
+      bulk_load(st, xb + (row0 + i) * a.x_stride, row_bytes, bar);
+      bulk_load(st + row_bytes, rb + (row0 + i) * a.r_stride, row_bytes, bar);
+    }
+  }
+  float inv_scale = 1.0f;
+  if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
+  const bool ok = mbar_wait_bounded(bar, 0);
+  const bool active = rr < nrows;
+  const int64_t row = row0 + rr;
+  const unsigned char* sx = smem + (size_t)rr * 2 * row_bytes;
+  const unsigned char* sr = sx + row_bytes;
+
+  float ss = 0.f;
+  if (ok && active) {
+    for (int v = rt; v < NV; v += tpr) {
+      float xf[8], rf[8];
+      unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
+      unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        xf[e] += rf[e];
+        ss += xf[e] * xf[e];
+      }
+      st_plain(rb + row * a.r_stride + (size_t)v * 8, pack8<T>(xf));
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+    pdl_launch_dependents();
+    return;
+  }
+  if (active) {
+    float tot = 0.f;
+    const int w0 = (rr * tpr) >> 5, nw = tpr >> 5;
+    for (int w = 0; w < nw; ++w) tot += red[w0 + w];
+    const float rstd = rsqrtf(tot * (1.0f / (float)H) + a.eps);
+    for (int v = rt; v < NV; v += tpr) {
+      float xf[8], rf[8], wf[8];
+      unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
+      unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
+      unpack8<T>(ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8), wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xf[e] = (xf[e] + rf[e]) * rstd * wf[e];
+      if constexpr (QUANT) {
+        uint2 q;
+        q.x = (uint32_t)f2_to_e4m3x2(xf[0] * inv_scale, xf[1] * inv_scale) |
+              ((uint32_t)f2_to_e4m3x2(xf[2] * inv_scale, xf[3] * inv_scale) << 16);
+        q.y = (uint32_t)f2_to_e4m3x2(xf[4] * inv_scale, xf[5] * inv_scale) |
+              ((uint32_t)f2_to_e4m3x2(xf[6] * inv_scale, xf[7] * inv_scale) << 16);
+        *reinterpret_cast<uint2*>(a.out + row * a.out_stride + (size_t)v * 8) = q;
+      } else {
+        st_plain(xb + row * a.x_stride + (size_t)v * 8, pack8<T>(xf));
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
 // Generic path: one CTA per row, scalar elements, any alignment.
 template <typename T, bool QUANT>
 __global__ void __launch_bounds__(256) norm_generic_kernel(const NormArgs a) {

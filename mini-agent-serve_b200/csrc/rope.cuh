@@ -126,6 +126,154 @@ __global__ void __launch_bounds__(kRopeThreads) rope_vec_kernel(const RopeArgs a
   pdl_launch_dependents();
 }
 
+// Token-staged ring (q heads and k heads each contiguous within a token, 16-byte aligned rows): a
+// persistent, warp-specialised TMA ring. Each CTA owns a contiguous block of tokens; their positions
+// are staged in shared memory up front (one coalesced read, validated there). Warp 0's first lane
+// streams, per token, the q row, the k row and the token's cos|sin cache row into an S-stage ring
+// with three bulk copies (cp.async.bulk, `full` mbarrier). The consumer warps rotate every pair of
+// the token from shared memory (cos/sin included), store the results to q/k with 16-byte stores,
+// and release the stage on its `empty` mbarrier. A token whose position is out of range gets no
+// copies and no stores. Every wait is bounded.
+struct RopeRingArgs {
+  const void* pos;
+  void* q;
+  void* k;
+  const float* cache;
+  int64_t T;
+  int64_t P;
+  int64_t qsn, ksn;          // token strides (elements); heads are contiguous (stride = head_size)
+  int32_t Hq, Hkv, D, rd;
+  int32_t stages;
+  int32_t tokens_per_cta;
+  int32_t* status;
+  int32_t* fault;
+};
+
+constexpr int kRopeConsumerWarps = 8;
+constexpr int kRopeRingThreads = 32 * (1 + kRopeConsumerWarps);
+constexpr int kRopeMaxTokensPerCta = 2048;
+
+__host__ __device__ inline uint32_t rope_stage_bytes(int Hq, int Hkv, int D, int rd, int elem_bytes) {
+  return (uint32_t)((Hq + Hkv) * D * elem_bytes + rd * 4);
+}
+__host__ __device__ inline size_t rope_ring_smem_bytes(uint32_t stage, int stages, int tokens_per_cta) {
+  return (size_t)stages * stage + (size_t)stages * 16 + (size_t)tokens_per_cta * 8;
+}
+
+template <typename T, typename PosT, bool NEOX>
+__global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeRingArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int S = a.stages;
+  const int NH = a.Hq + a.Hkv;
+  const uint32_t q_bytes = (uint32_t)(a.Hq * a.D) * (uint32_t)sizeof(T);
+  const uint32_t k_bytes = (uint32_t)(a.Hkv * a.D) * (uint32_t)sizeof(T);
+  const uint32_t c_bytes = (uint32_t)a.rd * 4u;
+  const uint32_t stage_bytes = q_bytes + k_bytes + c_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  uint64_t* empty = full + S;
+  int64_t* spos = reinterpret_cast<int64_t*>(empty + S);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const int64_t tok0 = (int64_t)blockIdx.x * a.tokens_per_cta;
+  const int n = (int)min((int64_t)a.tokens_per_cta, a.T - tok0);
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRopeConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  pdl_wait();
+  const PosT* pos_p = static_cast<const PosT*>(a.pos) + tok0;
+  for (int i = tid; i < n; i += kRopeRingThreads) {
+    const int64_t pos = (int64_t)pos_p[i];
+    const bool valid = pos >= 0 && pos < a.P;
+    if (!valid) flag_status(a.status, MAS_STATUS_ROPE_POS_OUT_OF_RANGE);
+    spos[i] = valid ? pos : -1;
+  }
+  __syncthreads();
+
+  T* const qb = static_cast<T*>(a.q);
+  T* const kb = static_cast<T*>(a.k);
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) {
+        const int s = i % S;
+        if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((i / S) - 1) & 1u)) {
+          atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+          break;
+        }
+        const int64_t pos = spos[i];
+        if (pos < 0) {
+          mbar_arrive(&full[s]);
+          continue;
+        }
+        unsigned char* st = smem + (size_t)s * stage_bytes;
+        const int64_t t = tok0 + i;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        if (q_bytes) bulk_load(st, qb + t * a.qsn, q_bytes, &full[s]);
+        if (k_bytes) bulk_load(st + q_bytes, kb + t * a.ksn, k_bytes, &full[s]);
+        bulk_load(st + q_bytes + k_bytes, a.cache + pos * a.rd, c_bytes, &full[s]);
+      }
+    }
+  } else {
+    const int ct = tid - 32;
+    constexpr int ncons = 32 * kRopeConsumerWarps;
+    const int tpu = a.rd >> 4;  // threads' worth of 8-pair groups per head
+    const int half = a.rd >> 1;
+    const int groups = NH * tpu;
+    for (int i = 0; i < n; ++i) {
+      const int s = i % S;
+      if (!mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u)) {
+        if (lane == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+        break;
+      }
+      if (spos[i] >= 0) {
+        const unsigned char* st = smem + (size_t)s * stage_bytes;
+        const float* c = reinterpret_cast<const float*>(st + q_bytes + k_bytes);
+        const int64_t t = tok0 + i;
+        for (int gi = ct; gi < groups; gi += ncons) {
+          const int h = gi / tpu;
+          const int j = gi - h * tpu;
+          const T* sh = reinterpret_cast<const T*>(st) + (size_t)h * a.D;  // staged head (q then k)
+          T* gh = h < a.Hq ? qb + t * a.qsn + (int64_t)h * a.D : kb + t * a.ksn + (int64_t)(h - a.Hq) * a.D;
+          const int off0 = NEOX ? j * 8 : j * 16;
+          const int off1 = NEOX ? half + j * 8 : j * 16 + 8;
+          float cs[8], sn[8], x0[8], x1[8], o0[8], o1[8];
+          {
+            const float4 c0 = *reinterpret_cast<const float4*>(c + j * 8);
+            const float4 c1 = *reinterpret_cast<const float4*>(c + j * 8 + 4);
+            const float4 s0 = *reinterpret_cast<const float4*>(c + half + j * 8);
+            const float4 s1 = *reinterpret_cast<const float4*>(c + half + j * 8 + 4);
+            cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+            cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+            sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+            sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+          }
+          unpack8<T>(*reinterpret_cast<const Vec16*>(sh + off0), x0);
+          unpack8<T>(*reinterpret_cast<const Vec16*>(sh + off1), x1);
+          if constexpr (NEOX) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) rotate(x0[e], x1[e], cs[e], sn[e], o0[e], o1[e]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              rotate(x0[2 * e], x0[2 * e + 1], cs[e], sn[e], o0[2 * e], o0[2 * e + 1]);
+              rotate(x1[2 * e], x1[2 * e + 1], cs[4 + e], sn[4 + e], o1[2 * e], o1[2 * e + 1]);
+            }
+          }
+          st_plain(gh + off0, pack8<T>(o0));
+          st_plain(gh + off1, pack8<T>(o1));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  pdl_launch_dependents();
+}
+
 // Generic path: one thread per rotation pair, scalar elements, any rotary_dim and alignment.
 template <typename T, typename PosT, bool NEOX>
 __global__ void __launch_bounds__(kRopeThreads) rope_generic_kernel(const RopeArgs a) {

@@ -35,7 +35,7 @@ struct SiluArgs {
 __device__ __forceinline__ float silu_f32(float v) { return v / (1.0f + __expf(-v)); }
 
 constexpr int kSiluThreads = 256;            // scalar path
-constexpr int kSiluConsumerWarps = 8;
+constexpr int kSiluConsumerWarps = 16;
 constexpr int kSiluRingThreads = 32 * (1 + kSiluConsumerWarps);
 constexpr int kSiluChunk = 4096;             // columns per tile: 8 KB of gate + 8 KB of up (bf16)
 
@@ -114,6 +114,29 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// Register variant: one 16-byte gate/up pair per thread (at most 42 registers, so 1536 threads per
+// SM keep 48 KB of loads in flight), a 2-D grid of (256-vector column blocks, rows).
+template <typename T>
+__global__ void __launch_bounds__(kSiluThreads, 6) silu_mul_vec_kernel(const SiluArgs a) {
+  pdl_wait();
+  const int nvec = a.d >> 3;
+  const int v = blockIdx.x * kSiluThreads + threadIdx.x;
+  if (v < nvec) {
+    for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
+      const T* g = static_cast<const T*>(a.in) + row * a.in_stride + (size_t)v * 8;
+      const Vec16 gv = ld_stream(g);
+      const Vec16 uv = ld_stream(g + a.d);
+      float gf[8], uf[8], y[8];
+      unpack8<T>(gv, gf);
+      unpack8<T>(uv, uf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = silu_f32(gf[e]) * uf[e];
+      st_plain(static_cast<T*>(a.out) + row * a.out_stride + (size_t)v * 8, pack8<T>(y));
     }
   }
   pdl_launch_dependents();

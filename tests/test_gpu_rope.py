@@ -64,6 +64,33 @@ def test_rope_partial_and_generic_rotary(cuda, D, rd):
     _run(cuda, 11, 3, 1, D, rd, 64)
 
 
+@pytest.mark.parametrize("neox", [True, False])
+def test_rope_padded_heads_vector_path(cuda, neox):
+    """Heads that are not contiguous within a token (head stride 2*D) take the per-unit vector kernel
+    instead of the token-staged ring; the padding between heads stays untouched."""
+    T, Hq, Hkv, D, P = 13, 3, 2, 128, 64
+    g = torch.Generator().manual_seed(21)
+    qbuf = torch.randn(T, Hq, 2 * D, generator=g).to(torch.bfloat16)
+    kbuf = torch.randn(T, Hkv, 2 * D, generator=g).to(torch.bfloat16)
+    ang = torch.rand(P, D // 2, generator=g) * 6.283185307179586
+    cache = torch.cat([ang.cos(), ang.sin()], dim=-1).float()
+    pos = torch.randint(0, P, (T,), generator=g).to(torch.int32)
+    qd, kd = qbuf.to(cuda), kbuf.to(cuda)
+    q, k = qd[..., :D], kd[..., :D]
+    rc = mas_b200._lib.lib.mas_rope_cos_sin_cache_inplace(
+        pos.to(cuda).data_ptr(), 4, q.data_ptr(), k.data_ptr(), cache.to(cuda).data_ptr(), T, Hq, Hkv, D, D, P,
+        q.stride(0), q.stride(1), k.stride(0), k.stride(1), int(neox), 0, None, 1,
+        torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, mas_b200.status_string(rc)
+    # the oracle takes (tokens, heads*D) views; feed it compact copies and compare the rotated parts
+    qc, kc = qbuf[..., :D].contiguous().view(T, -1), kbuf[..., :D].contiguous().view(T, -1)
+    oracle.apply_rope_with_cos_sin_cache_inplace(pos, qc, kc, D, cache, is_neox=neox)
+    assert_ulp(qd[..., :D].cpu().contiguous().view(T, -1), qc, what="padded q")
+    assert_ulp(kd[..., :D].cpu().contiguous().view(T, -1), kc, what="padded k")
+    assert_bits_equal(qd[..., D:].cpu(), qbuf[..., D:], "q padding")
+    assert_bits_equal(kd[..., D:].cpu(), kbuf[..., D:], "k padding")
+
+
 def test_rope_out_of_range_positions_flagged(cuda):
     T, Hq, Hkv, D, P = 6, 2, 1, 128, 32
     qkv, cache, pos = _case(T, Hq, Hkv, D, D, P)
