@@ -6,6 +6,7 @@
 // of the fault word), done once per device under a lock.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -78,6 +79,8 @@ cudaError_t prepare_current(DeviceState& st, int device) {
   if ((e = opt_in_smem(norm_row_kernel<__nv_bfloat16, true>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(norm_row_kernel<__half, false>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(norm_row_kernel<__half, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(silu_mul_async_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(silu_mul_async_kernel<__half>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__half>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int32_t, true>)) != cudaSuccess) return e;
@@ -234,24 +237,33 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
   }
   if (fast_ok && H % 8 == 0) {
     const int nv = H / 8;
-    const int vpt = (int)ceil_div(nv, kNormMaxConsumers);
-    const int nt = 32 + (int)ceil_div(ceil_div(nv, vpt), 32) * 32;  // producer warp + consumers
+    static const int env_groups = env_int("MAS_NORM_GROUPS", 0);
+    const int groups = std::max(1, std::min(kNormMaxGroups, env_groups > 0 ? env_groups : 2));
+    const int vpt = (int)ceil_div(nv, kNormMaxConsumers / groups);
+    const int gsize = (int)ceil_div(ceil_div(nv, vpt), 32) * 32;
+    const int nt = 32 + groups * gsize;  // producer warp + consumer groups
+    a.groups = groups;
     const size_t stage = 2ull * (size_t)H * sizeof(T);
     static const int env_ctas = env_int("MAS_NORM_CTAS_PER_SM", 0);
     static const int env_stages = env_int("MAS_NORM_STAGES", 0);
-    // Ring depth first: a stage is refilled one row after it is consumed, so S stages keep S-1 rows
-    // in flight per CTA; 4 stages hide the load latency behind three rows of work. Then as many CTAs
-    // per SM as the ring budget and the thread limit allow, and any budget left deepens the ring.
+    // Ring depth first (4 stages), then as many CTAs per SM as the ring budget, the thread limit and
+    // the occupancy (registers) allow; budget left over deepens the ring (up to 8 stages).
+    const void* fn = norm_tma_fn<T, Q>(vpt);
     int stages = env_stages > 0 ? env_stages : 4;
     if ((size_t)stages * stage > kRingBytesPerSm) stages = (int)std::max<size_t>(2, kRingBytesPerSm / stage);
-    int ctas = env_ctas > 0 ? env_ctas : (int)std::max<size_t>(1, kRingBytesPerSm / ((size_t)stages * stage));
-    ctas = std::max(1, std::min(ctas, 2048 / nt));
-    if (env_stages <= 0) stages = (int)std::max<size_t>(stages, std::min<size_t>(8, kRingBytesPerSm / ((size_t)ctas * stage)));
     stages = std::max(2, std::min(8, stages));
-    const size_t smem = norm_tma_smem_bytes(H, stages, (int)sizeof(T));
-    const void* fn = norm_tma_fn<T, Q>(vpt);
+    size_t smem = norm_tma_smem_bytes(H, stages, (int)sizeof(T));
     if (fn != nullptr && smem <= kMaxSmemPerCta) {
-      ctas = std::min(ctas, resident_ctas(fn, nt, smem));  // the grid must be fully resident
+      int ctas = env_ctas > 0 ? env_ctas : (int)std::max<size_t>(1, kRingBytesPerSm / ((size_t)stages * stage));
+      ctas = std::max(1, std::min({ctas, 2048 / nt, resident_ctas(fn, nt, smem)}));
+      if (env_stages <= 0) {
+        const int deeper = (int)std::min<size_t>(8, kRingBytesPerSm / ((size_t)ctas * stage));
+        if (deeper > stages && norm_tma_smem_bytes(H, deeper, (int)sizeof(T)) <= kMaxSmemPerCta) {
+          stages = deeper;
+          smem = norm_tma_smem_bytes(H, stages, (int)sizeof(T));
+          ctas = std::max(1, std::min(ctas, resident_ctas(fn, nt, smem)));  // the grid must stay resident
+        }
+      }
       int64_t grid = std::min<int64_t>(a.rows, (int64_t)st.sm_count * ctas);
       a.rows_per_cta = (int32_t)ceil_div(a.rows, grid);
       grid = ceil_div(a.rows, a.rows_per_cta);
@@ -370,6 +382,22 @@ int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
   const bool vec = d % 8 == 0 && aligned(out, 16) && aligned(input, 16) && input_stride % 8 == 0 &&
                    out_stride % 8 == 0;
   static const bool use_vec = env_is("MAS_SILU_IMPL", "vec");
+  static const bool use_ring = env_is("MAS_SILU_IMPL", "ring");
+  if (vec && !use_vec && !use_ring) {
+    // Per-thread cp.async pipeline: column blocks of 256 vectors x row groups, every CTA resident.
+    const void* fn = dtype == MAS_DTYPE_BF16 ? (const void*)silu_mul_async_kernel<__nv_bfloat16>
+                                             : (const void*)silu_mul_async_kernel<__half>;
+    const size_t smem = silu_async_smem_bytes();
+    const int ctas = resident_ctas(fn, kSiluAsyncThreads, smem);
+    const int64_t gx = ceil_div(d / 8, kSiluAsyncThreads);
+    int64_t gy = std::min<int64_t>(num_tokens, 65535);
+    gy = std::max<int64_t>(1, std::min<int64_t>(gy, (int64_t)st->sm_count * ctas / std::max<int64_t>(1, gx)));
+    if (dtype == MAS_DTYPE_BF16)
+      return launch(silu_mul_async_kernel<__nv_bfloat16>, dim3((unsigned)gx, (unsigned)gy), dim3(kSiluAsyncThreads),
+                    smem, stream, enable_pdl, a);
+    return launch(silu_mul_async_kernel<__half>, dim3((unsigned)gx, (unsigned)gy), dim3(kSiluAsyncThreads), smem,
+                  stream, enable_pdl, a);
+  }
   if (vec && use_vec) {
     const unsigned gx = (unsigned)ceil_div(d / 8, kSiluThreads);
     const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, 65535);

@@ -10,11 +10,12 @@
 // TMA ring. Each CTA owns a contiguous block of rows. Warp 0 is the producer: one lane streams whole
 // rows of x and r into an S-stage shared-memory ring with two bulk copies per row (cp.async.bulk,
 // completion on the stage's `full` mbarrier), refilling a stage as soon as every consumer warp has
-// released it on the stage's `empty` mbarrier. The consumer warps each own the same VPT 16-byte
-// column slots of every row: they wait on `full`, form h = x + r in registers, store round(h) to
-// the residual, reduce sum(h^2) through warp shuffles and one named barrier among consumers, store
-// the normalised row, and release the stage. The weight slice lives in registers for the whole
-// kernel. Every wait is bounded.
+// released it on the stage's `empty` mbarrier. The consumer warps form `groups` groups; group g takes
+// rows g, g + groups, ..., so that many rows are in their reduction phase at once. Within a group
+// each thread owns the same VPT 16-byte column slots of every row: it waits on `full`, forms
+// h = x + r in registers, stores round(h) to the residual, releases the stage, reduces sum(h^2)
+// through warp shuffles and one named barrier of its group, and stores the normalised row. The
+// weight slice lives in registers for the whole kernel. Every wait is bounded.
 //
 // Generic path (any H, stride or alignment): one CTA per row, two passes over global memory; the
 // second pass recomputes h from the still-unmodified inputs, so no scratch space is needed.
@@ -37,6 +38,7 @@ struct NormArgs {
   int32_t H;
   int32_t stages;       // ring depth (fast path)
   int32_t rows_per_cta; // fast path
+  int32_t groups;       // fast path: consumer groups per CTA (rows k = g, g + groups, ... per group)
   float eps;
   int32_t* fault;       // library fault word (bulk-copy timeouts)
 };
@@ -44,21 +46,24 @@ struct NormArgs {
 constexpr int kNormMaxWarps = 32;
 
 // Shared-memory bytes of the fast path for one CTA.
+constexpr int kNormMaxGroups = 4;
+
 __host__ __device__ inline size_t norm_tma_smem_bytes(int H, int stages, int elem_bytes) {
   const size_t stage = 2ull * (size_t)H * (size_t)elem_bytes;
-  return (size_t)stages * stage + (size_t)stages * 16 + 2 * kNormMaxWarps * sizeof(float);
+  return (size_t)stages * stage + (size_t)stages * 16 + kNormMaxGroups * 2 * kNormMaxWarps * sizeof(float);
 }
 
-// Named barrier 1 over the consumer warps, OR-reducing a predicate (the producer never joins it).
-__device__ __forceinline__ bool consumers_sync_or(bool pred, int nthreads) {
+// Named barrier `id` (1 + consumer group) over one group's warps, OR-reducing a predicate (the
+// producer warp and the other groups never join it).
+__device__ __forceinline__ bool group_sync_or(int id, bool pred, int nthreads) {
   uint32_t out;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(out)
-      : "r"((uint32_t)pred), "r"(nthreads)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
       : "memory");
   return out != 0;
 }
@@ -79,8 +84,9 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int ncons = blockDim.x - 32;  // consumer threads
-  const int ncw = ncons >> 5;
+  const int G = a.groups;
+  const int gsize = (blockDim.x - 32) / G;  // threads per consumer group (a multiple of 32)
+  const int gw = gsize >> 5;                // warps per group
 
   const int64_t row0 = (int64_t)blockIdx.x * a.rows_per_cta;
   const int n = (int)min((int64_t)a.rows_per_cta, a.rows - row0);
@@ -88,7 +94,7 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], ncw);
+      mbar_init(&empty[s], gw);  // each row is consumed by exactly one group
     }
     fence_barrier_init();
   }
@@ -113,80 +119,101 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
       }
     }
   } else {
-    const int ct = tid - 32;
-    const int cw = warp - 1;
+    const int g = (tid - 32) / gsize;   // consumer group
+    const int ct = tid - 32 - g * gsize;  // thread index within the group
+    const int cw = ct >> 5;
     // This thread's slice of the weight, for every row.
     Vec16 wv[VPT];
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
-      const int v = ct + j * ncons;
+      const int v = ct + j * gsize;
       if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
     }
     float inv_scale = 1.0f;
     if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
     const float inv_h = 1.0f / (float)H;
+    float* gred = red + g * 2 * kNormMaxWarps;
 
-    for (int k = 0; k < n; ++k) {
+    for (int k = g; k < n; k += G) {
       const int s = k % S;
       const bool ok = mbar_wait_bounded(&full[s], (uint32_t)(k / S) & 1u);
       const unsigned char* sx = ring + (size_t)s * 2 * row_bytes;
       const unsigned char* sr = sx + row_bytes;
       const int64_t row = row0 + k;
 
-      // h = x + r (kept in registers), residual <- round(h), sum of h^2.
-      float h[VPT][8];
+      // h = x + r, residual <- round(h), sum of h^2. With few columns per thread h stays in
+      // registers and the stage is released at once; otherwise h is re-read from the stage in the
+      // second pass and the stage is released after it.
+      constexpr bool kKeepH = VPT <= 4;
+      float h[kKeepH ? VPT : 1][8];
       float ss = 0.f;
       if (ok) {
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
-          const int v = ct + j * ncons;
+          const int v = ct + j * gsize;
           if (v < NV) {
-            float rf[8];
-            unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), h[j]);
+            float xf[8], rf[8];
+            unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
             unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              h[j][e] += rf[e];
-              ss += h[j][e] * h[j][e];
+              xf[e] += rf[e];
+              ss += xf[e] * xf[e];
+              if constexpr (kKeepH) h[j][e] = xf[e];
             }
-            st_plain(rb + row * a.r_stride + (size_t)v * 8, pack8<T>(h[j]));
+            st_plain(rb + row * a.r_stride + (size_t)v * 8, pack8<T>(xf));
           }
         }
       }
-      // The staged row is no longer read: hand the stage back to the producer.
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if constexpr (kKeepH) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+      }
 
       ss = warp_sum(ss);
-      float* red_k = red + (k & 1) * kNormMaxWarps;
+      float* red_k = gred + ((k / G) & 1) * kNormMaxWarps;
       if (lane == 0) red_k[cw] = ss;
-      if (consumers_sync_or(!ok, ncons)) {
+      if (group_sync_or(1 + g, !ok, gsize)) {
         if (ct == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
         break;
       }
       float tot = 0.f;
-      for (int w = 0; w < ncw; ++w) tot += red_k[w];
+      for (int w = 0; w < gw; ++w) tot += red_k[w];
       const float rstd = rsqrtf(tot * inv_h + a.eps);
 
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        const int v = ct + j * ncons;
+        const int v = ct + j * gsize;
         if (v < NV) {
-          float wf[8];
+          float y[8], wf[8];
+          if constexpr (kKeepH) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) y[e] = h[j][e];
+          } else {
+            float rf[8];
+            unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), y);
+            unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) y[e] += rf[e];
+          }
           unpack8<T>(wv[j], wf);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) h[j][e] = h[j][e] * rstd * wf[e];
+          for (int e = 0; e < 8; ++e) y[e] = y[e] * rstd * wf[e];
           if constexpr (QUANT) {
             uint2 q;
-            q.x = (uint32_t)f2_to_e4m3x2(h[j][0] * inv_scale, h[j][1] * inv_scale) |
-                  ((uint32_t)f2_to_e4m3x2(h[j][2] * inv_scale, h[j][3] * inv_scale) << 16);
-            q.y = (uint32_t)f2_to_e4m3x2(h[j][4] * inv_scale, h[j][5] * inv_scale) |
-                  ((uint32_t)f2_to_e4m3x2(h[j][6] * inv_scale, h[j][7] * inv_scale) << 16);
+            q.x = (uint32_t)f2_to_e4m3x2(y[0] * inv_scale, y[1] * inv_scale) |
+                  ((uint32_t)f2_to_e4m3x2(y[2] * inv_scale, y[3] * inv_scale) << 16);
+            q.y = (uint32_t)f2_to_e4m3x2(y[4] * inv_scale, y[5] * inv_scale) |
+                  ((uint32_t)f2_to_e4m3x2(y[6] * inv_scale, y[7] * inv_scale) << 16);
             *reinterpret_cast<uint2*>(a.out + row * a.out_stride + (size_t)v * 8) = q;
           } else {
-            st_plain(xb + row * a.x_stride + (size_t)v * 8, pack8<T>(h[j]));
+            st_plain(xb + row * a.x_stride + (size_t)v * 8, pack8<T>(y));
           }
         }
+      }
+      if constexpr (!kKeepH) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
       }
     }
   }

@@ -87,6 +87,14 @@ def main(out_dir: Path) -> None:
             out = silu_and_mul(xin.to(dev), enable_pdl=True)
             torch.cuda.synchronize()
             arrays.update({f"silu_{name}_in": bits(xin), f"silu_{name}_out": bits(out)})
+        # Gate values down to -100 (where 1 + exp(-v) passes 2^126 and then overflows): pins how the
+        # fp32 quotient of the activation behaves at the edge of its range.
+        gate = -torch.linspace(60.0, 100.0, 2048)
+        up = 1 + torch.rand(2048, generator=g)
+        xin = torch.cat([gate, up]).view(1, -1).to(torch.bfloat16)
+        out = silu_and_mul(xin.to(dev), enable_pdl=True)
+        torch.cuda.synchronize()
+        arrays.update({"silu_sneg_in": bits(xin), "silu_sneg_out": bits(out)})
     except Exception:
         failures.append("silu_and_mul: " + traceback.format_exc(limit=2))
 

@@ -76,9 +76,10 @@ def test_rope_padded_heads_vector_path(cuda, neox):
     cache = torch.cat([ang.cos(), ang.sin()], dim=-1).float()
     pos = torch.randint(0, P, (T,), generator=g).to(torch.int32)
     qd, kd = qbuf.to(cuda), kbuf.to(cuda)
+    pos_d, cache_d = pos.to(cuda), cache.to(cuda)  # kept alive until the kernel has run
     q, k = qd[..., :D], kd[..., :D]
     rc = mas_b200._lib.lib.mas_rope_cos_sin_cache_inplace(
-        pos.to(cuda).data_ptr(), 4, q.data_ptr(), k.data_ptr(), cache.to(cuda).data_ptr(), T, Hq, Hkv, D, D, P,
+        pos_d.data_ptr(), 4, q.data_ptr(), k.data_ptr(), cache_d.data_ptr(), T, Hq, Hkv, D, D, P,
         q.stride(0), q.stride(1), k.stride(0), k.stride(1), int(neox), 0, None, 1,
         torch.cuda.current_stream().cuda_stream)
     assert rc == 0, mas_b200.status_string(rc)
