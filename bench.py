@@ -369,9 +369,11 @@ class OpWorkload:
 
     def step(self, dom_events=None):
         st = torch.cuda.current_stream()
-        # Evict the previous launch's data from L2 (a 256 MB write) outside the launch's events, so
-        # each launch reads its inputs from HBM.
+        # Evict the previous launch's data from L2 outside the launch's events: a 256 MB write, then a
+        # read of the same buffer so that the lines L2 is left holding are clean (no write-back of the
+        # flush itself lands inside the timed launch). Each launch then reads its inputs from HBM.
         self.flush.zero_()
+        self.flush_sum = self.flush.sum(dtype=torch.int32)
         if dom_events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)

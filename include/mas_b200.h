@@ -133,6 +133,25 @@ MAS_API int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_
                                    int dtype, int32_t* status, int enable_pdl, void* stream);
 
 /*
+ * Rotary embedding as mas_rope_cos_sin_cache_inplace, fused with the llama-4 query scale that
+ * Devstral2Attention.forward applies after it (miniagentserve/models/devstral2/devstral2.py:175-179):
+ *   scale = round(1 + beta * log1p(floor(pos * (1 / original_max))))   (fp32 steps, each rounded)
+ *   q <- round(round(rotated q) * scale)            for every element of every q head
+ * k is rotated only. The reference computes the scale as a separate tensor and multiplies q out of
+ * place; here q is scaled in place (its unscaled value is not used after the scale in the reference).
+ * `1 / original_max` is the fp32 reciprocal, as torch evaluates `tensor / host_scalar` on CUDA.
+ * q_scale_original_max must be positive; q_scale_beta == 0 gives mas_rope_cos_sin_cache_inplace.
+ */
+MAS_API int mas_rope_cos_sin_cache_q_scale_inplace(const void* positions, int positions_dtype, void* query,
+                                                   void* key, const float* cos_sin_cache, int64_t num_tokens,
+                                                   int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                                                   int64_t rotary_dim, int64_t max_positions,
+                                                   int64_t q_stride_token, int64_t q_stride_head,
+                                                   int64_t k_stride_token, int64_t k_stride_head, int is_neox,
+                                                   float q_scale_beta, int64_t q_scale_original_max, int dtype,
+                                                   int32_t* status, int enable_pdl, void* stream);
+
+/*
  * Token-embedding gather: out[t, :] = table[ids[t], :] (a bit copy of hidden_size elements of
  * elem_size bytes). ids: int32 or int64 (ids_dtype). An id outside [0, vocab_size) zeroes its output
  * row and sets MAS_STATUS_EMBED_ID_OUT_OF_RANGE in *status when status is not NULL.
@@ -143,6 +162,20 @@ MAS_API int mas_embedding_gather(void* out, const void* table, const void* ids, 
                          int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
                          int64_t out_stride, int64_t table_stride, int elem_size,
                          int32_t* status, int enable_pdl, void* stream);
+
+/*
+ * Token-embedding gather fused with ModelRunner.fill_placeholders
+ * (miniagentserve/engine/model_runner.py:149-154): an id -1-r (r >= 0) is a placeholder for
+ * last_tokens[r], the previous step's sample of row r. Each placeholder is resolved, the resolved id
+ * is written back into `ids` (as fill_placeholders does), and the row of the resolved id is gathered,
+ * all in one launch. last_tokens: int32 or int64 (last_dtype), num_last entries. A placeholder whose r
+ * is not below num_last is an out-of-range id (zero row, MAS_STATUS_EMBED_ID_OUT_OF_RANGE).
+ */
+MAS_API int mas_embedding_gather_fill_placeholders(void* out, const void* table, void* ids, int ids_dtype,
+                                                   const void* last_tokens, int last_dtype, int64_t num_last,
+                                                   int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
+                                                   int64_t out_stride, int64_t table_stride, int elem_size,
+                                                   int32_t* status, int enable_pdl, void* stream);
 
 #ifdef __cplusplus
 }

@@ -21,8 +21,10 @@ from . import _lib, ops, rope_cache, embedding, chain, workloads  # noqa: F401
 from ._lib import MasError, prepare_device, read_fault_word, status_string, version
 from .embedding import Embedding
 from .ops import (
+    apply_rope_and_llama4_query_scale_inplace,
     apply_rope_with_cos_sin_cache_inplace,
     embedding as embedding_gather,
+    embedding_fill_placeholders,
     embedding_out,
     fused_add_rmsnorm,
     fused_add_rmsnorm_quant,
@@ -35,8 +37,10 @@ from .rope_cache import plain_cos_sin_cache, yarn_cos_sin_cache
 __all__ = [
     "Embedding",
     "MasError",
+    "apply_rope_and_llama4_query_scale_inplace",
     "apply_rope_with_cos_sin_cache_inplace",
     "chain",
+    "embedding_fill_placeholders",
     "embedding_gather",
     "embedding_out",
     "fused_add_rmsnorm",

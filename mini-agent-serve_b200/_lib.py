@@ -48,8 +48,13 @@ SIGNATURES: dict[str, tuple[type, list[type]]] = {
     "mas_rope_cos_sin_cache_inplace": (
         _i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                _i32, _i32, _vp, _i32, _vp]),
+    "mas_rope_cos_sin_cache_q_scale_inplace": (
+        _i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+               _i32, _f32, _i64, _i32, _vp, _i32, _vp]),
     "mas_embedding_gather": (
         _i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _i32, _vp]),
+    "mas_embedding_gather_fill_placeholders": (
+        _i32, [_vp, _vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _i32, _vp]),
 }
 
 

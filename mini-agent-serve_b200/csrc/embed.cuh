@@ -31,7 +31,29 @@ struct EmbedArgs {
   int32_t rows_per_cta;
   int32_t* status;
   int32_t* fault;
+  // Placeholder filling (ModelRunner.fill_placeholders, model_runner.py:149-154): when `last` is set,
+  // an id -1-r (r >= 0) stands for last[r], the previous step's sample for row r; the resolved id is
+  // written back into ids. r outside [0, n_last) is an out-of-range id.
+  const void* last;
+  int64_t n_last;
+  int32_t last_is_64;
 };
+
+// The id of token t, with a placeholder resolved (and written back) when placeholder filling is on.
+template <typename IdT>
+__device__ __forceinline__ int64_t resolve_id(const EmbedArgs& a, const IdT* ids, int64_t t) {
+  int64_t id = (int64_t)ids[t];
+  if (a.last != nullptr && id < 0) {
+    const int64_t r = -1 - id;
+    if (r < a.n_last) {
+      id = a.last_is_64 ? static_cast<const int64_t*>(a.last)[r] : (int64_t) static_cast<const int32_t*>(a.last)[r];
+      const_cast<IdT*>(ids)[t] = (IdT)id;
+    } else {
+      id = -1;
+    }
+  }
+  return id;
+}
 
 constexpr int kEmbedMaxRowsPerCta = 1024;
 
@@ -59,7 +81,7 @@ __global__ void __launch_bounds__(32) embed_tma_kernel(const EmbedArgs a) {
   pdl_wait();
   const IdT* ids = static_cast<const IdT*>(a.ids) + row0;
   for (int i = lane; i < n; i += kWarp) {
-    const int64_t id = (int64_t)ids[i];
+    const int64_t id = resolve_id<IdT>(a, ids, i);
     const bool valid = id >= 0 && id < a.V;
     if (!valid) flag_status(a.status, MAS_STATUS_EMBED_ID_OUT_OF_RANGE);
     sid[i] = valid ? id : -1;
@@ -134,7 +156,9 @@ __global__ void __launch_bounds__(256) embed_generic_kernel(const EmbedArgs a, i
   const unsigned char* table = static_cast<const unsigned char*>(a.table);
   unsigned char* out = static_cast<unsigned char*>(a.out);
   for (int64_t t = wid; t < a.T; t += nw) {
-    const int64_t id = (int64_t)ids[t];
+    int64_t id = 0;
+    if (lane == 0) id = resolve_id<IdT>(a, ids, t);
+    id = __shfl_sync(0xffffffffu, id, 0);
     const bool valid = id >= 0 && id < a.V;
     if (!valid && lane == 0) flag_status(a.status, MAS_STATUS_EMBED_ID_OUT_OF_RANGE);
     const unsigned char* src = table + (valid ? id : 0) * a.table_stride_b;

@@ -68,6 +68,15 @@ cudaError_t opt_in_norm() {
   return e;
 }
 
+template <typename T, bool Q>
+cudaError_t opt_in_norm_row() {
+  cudaError_t e = opt_in_smem(norm_row_kernel<T, Q, 4>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_kernel<T, Q, 8>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_kernel<T, Q, 12>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_kernel<T, Q, 16>);
+  return e;
+}
+
 cudaError_t prepare_current(DeviceState& st, int device) {
   cudaError_t e = cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return e;
@@ -75,10 +84,10 @@ cudaError_t prepare_current(DeviceState& st, int device) {
   if ((e = opt_in_norm<__nv_bfloat16, true>()) != cudaSuccess) return e;
   if ((e = opt_in_norm<__half, false>()) != cudaSuccess) return e;
   if ((e = opt_in_norm<__half, true>()) != cudaSuccess) return e;
-  if ((e = opt_in_smem(norm_row_kernel<__nv_bfloat16, false>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(norm_row_kernel<__nv_bfloat16, true>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(norm_row_kernel<__half, false>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(norm_row_kernel<__half, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_norm_row<__nv_bfloat16, false>()) != cudaSuccess) return e;
+  if ((e = opt_in_norm_row<__nv_bfloat16, true>()) != cudaSuccess) return e;
+  if ((e = opt_in_norm_row<__half, false>()) != cudaSuccess) return e;
+  if ((e = opt_in_norm_row<__half, true>()) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_async_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_async_kernel<__half>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
@@ -229,10 +238,16 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
     cta = std::max(tpr, std::min(cta, kNormRowMaxThreads)) / tpr * tpr;
     const int rpc = cta / tpr;
     const size_t smem = norm_row_smem_bytes(H, rpc, (int)sizeof(T));
-    if (smem <= kMaxSmemPerCta) {
+    const int vpt = (int)ceil_div(H / 8, tpr);
+    if (smem <= kMaxSmemPerCta && vpt <= 16) {
       const int64_t grid = ceil_div(a.rows, rpc);
-      if (grid <= INT32_MAX)
-        return launch(norm_row_kernel<T, Q>, dim3((unsigned)grid), dim3(cta), smem, stream, pdl, a, tpr, rpc);
+      const dim3 g((unsigned)grid), b(cta);
+      if (grid <= INT32_MAX) {
+        if (vpt <= 4) return launch(norm_row_kernel<T, Q, 4>, g, b, smem, stream, pdl, a, tpr, rpc);
+        if (vpt <= 8) return launch(norm_row_kernel<T, Q, 8>, g, b, smem, stream, pdl, a, tpr, rpc);
+        if (vpt <= 12) return launch(norm_row_kernel<T, Q, 12>, g, b, smem, stream, pdl, a, tpr, rpc);
+        return launch(norm_row_kernel<T, Q, 16>, g, b, smem, stream, pdl, a, tpr, rpc);
+      }
     }
   }
   if (fast_ok && H % 8 == 0) {
@@ -432,13 +447,13 @@ int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
   return launch(silu_mul_generic_kernel<__half>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
 }
 
-int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, void* query,
-                                   void* key, const float* cos_sin_cache, int64_t num_tokens,
-                                   int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
-                                   int64_t rotary_dim, int64_t max_positions,
-                                   int64_t q_stride_token, int64_t q_stride_head,
-                                   int64_t k_stride_token, int64_t k_stride_head, int is_neox,
-                                   int dtype, int32_t* status, int enable_pdl, void* stream) {
+// Rotation (and, when q_beta != 0, the llama-4 query scale) of every rotary pair: one launch.
+static int rope_main(const void* positions, int positions_dtype, void* query, void* key,
+                     const float* cos_sin_cache, int64_t num_tokens, int64_t num_q_heads,
+                     int64_t num_kv_heads, int64_t head_size, int64_t rotary_dim,
+                     int64_t max_positions, int64_t q_stride_token, int64_t q_stride_head,
+                     int64_t k_stride_token, int64_t k_stride_head, int is_neox, int dtype,
+                     int32_t* status, int enable_pdl, void* stream, float q_beta, float q_inv_orig) {
   if (num_tokens < 0 || num_q_heads < 0 || num_kv_heads < 0 || head_size <= 0 ||
       max_positions < 0 || num_q_heads + num_kv_heads > INT32_MAX)
     return MAS_ERR_INVALID_ARGUMENT;
@@ -458,7 +473,7 @@ int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, v
   a.T = num_tokens; a.P = max_positions;
   a.qsn = q_stride_token; a.qsh = q_stride_head; a.ksn = k_stride_token; a.ksh = k_stride_head;
   a.Hq = (int32_t)num_q_heads; a.Hkv = (int32_t)num_kv_heads; a.rd = (int32_t)rotary_dim;
-  a.status = status;
+  a.status = status; a.q_beta = q_beta; a.q_inv_orig = q_inv_orig;
   const bool q_al = num_q_heads == 0 || (aligned(query, 16) && q_stride_token % 8 == 0 && q_stride_head % 8 == 0);
   const bool k_al = num_kv_heads == 0 || (aligned(key, 16) && k_stride_token % 8 == 0 && k_stride_head % 8 == 0);
   const bool vec = rotary_dim % 16 == 0 && rotary_dim / 16 <= 32 && q_al && k_al &&
@@ -490,6 +505,7 @@ int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, v
     r.pos = positions; r.q = query; r.k = key; r.cache = cos_sin_cache; r.T = num_tokens; r.P = max_positions;
     r.qsn = q_stride_token; r.ksn = k_stride_token; r.Hq = (int32_t)num_q_heads; r.Hkv = (int32_t)num_kv_heads;
     r.D = (int32_t)head_size; r.rd = (int32_t)rotary_dim; r.status = status; r.fault = st->fault;
+    r.q_beta = q_beta; r.q_inv_orig = q_inv_orig;
     const uint32_t stage = rope_stage_bytes(r.Hq, r.Hkv, r.D, r.rd, 2);
     static const int env_stages = env_int("MAS_ROPE_STAGES", 0);
     const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
@@ -536,10 +552,55 @@ int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, v
 #undef MAS_ROPE_LAUNCH
 }
 
-int mas_embedding_gather(void* out, const void* table, const void* ids, int ids_dtype,
-                         int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
-                         int64_t out_stride, int64_t table_stride, int elem_size,
-                         int32_t* status, int enable_pdl, void* stream) {
+int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, void* query,
+                                   void* key, const float* cos_sin_cache, int64_t num_tokens,
+                                   int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                                   int64_t rotary_dim, int64_t max_positions,
+                                   int64_t q_stride_token, int64_t q_stride_head,
+                                   int64_t k_stride_token, int64_t k_stride_head, int is_neox,
+                                   int dtype, int32_t* status, int enable_pdl, void* stream) {
+  return rope_main(positions, positions_dtype, query, key, cos_sin_cache, num_tokens, num_q_heads,
+                   num_kv_heads, head_size, rotary_dim, max_positions, q_stride_token, q_stride_head,
+                   k_stride_token, k_stride_head, is_neox, dtype, status, enable_pdl, stream, 0.f, 0.f);
+}
+
+int mas_rope_cos_sin_cache_q_scale_inplace(const void* positions, int positions_dtype, void* query,
+                                           void* key, const float* cos_sin_cache, int64_t num_tokens,
+                                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                                           int64_t rotary_dim, int64_t max_positions,
+                                           int64_t q_stride_token, int64_t q_stride_head,
+                                           int64_t k_stride_token, int64_t k_stride_head, int is_neox,
+                                           float q_scale_beta, int64_t q_scale_original_max, int dtype,
+                                           int32_t* status, int enable_pdl, void* stream) {
+  if (q_scale_original_max <= 0) return MAS_ERR_INVALID_ARGUMENT;
+  // torch divides a CUDA tensor by a host scalar as a multiplication by the fp32 reciprocal.
+  const float inv_orig = 1.0f / (float)q_scale_original_max;
+  int rc = rope_main(positions, positions_dtype, query, key, cos_sin_cache, num_tokens, num_q_heads,
+                     num_kv_heads, head_size, rotary_dim, max_positions, q_stride_token, q_stride_head,
+                     k_stride_token, k_stride_head, is_neox, dtype, status, enable_pdl, stream,
+                     q_scale_beta, inv_orig);
+  if (rc != MAS_OK || q_scale_beta == 0.f || rotary_dim >= head_size || num_q_heads == 0 || num_tokens == 0)
+    return rc;
+  // Partial rotary: the elements past rotary_dim are scaled by a second, element-wise launch.
+  RopeArgs a = {};
+  a.pos = positions; a.q = query; a.T = num_tokens; a.P = max_positions; a.qsn = q_stride_token;
+  a.qsh = q_stride_head; a.Hq = (int32_t)num_q_heads; a.rd = (int32_t)rotary_dim;
+  a.q_beta = q_scale_beta; a.q_inv_orig = inv_orig;
+  const int64_t total = num_tokens * num_q_heads * (head_size - rotary_dim);
+  const dim3 grid((unsigned)std::min<int64_t>(ceil_div(total, kRopeThreads), 1 << 22));
+  const bool bf = dtype == MAS_DTYPE_BF16, i64 = positions_dtype == MAS_DTYPE_INT64;
+  const int32_t hs = (int32_t)head_size;
+  if (bf) return i64 ? launch(rope_q_tail_scale_kernel<__nv_bfloat16, int64_t>, grid, dim3(kRopeThreads), 0, stream, enable_pdl, a, hs)
+                     : launch(rope_q_tail_scale_kernel<__nv_bfloat16, int32_t>, grid, dim3(kRopeThreads), 0, stream, enable_pdl, a, hs);
+  return i64 ? launch(rope_q_tail_scale_kernel<__half, int64_t>, grid, dim3(kRopeThreads), 0, stream, enable_pdl, a, hs)
+             : launch(rope_q_tail_scale_kernel<__half, int32_t>, grid, dim3(kRopeThreads), 0, stream, enable_pdl, a, hs);
+}
+
+static int gather_impl(void* out, const void* table, const void* ids, int ids_dtype,
+                       int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
+                       int64_t out_stride, int64_t table_stride, int elem_size,
+                       int32_t* status, int enable_pdl, void* stream, const void* last,
+                       int last_dtype, int64_t num_last) {
   if (num_tokens < 0 || hidden_size <= 0 || vocab_size < 0) return MAS_ERR_INVALID_ARGUMENT;
   if (elem_size != 1 && elem_size != 2 && elem_size != 4 && elem_size != 8) return MAS_ERR_UNSUPPORTED_DTYPE;
   if (ids_dtype != MAS_DTYPE_INT32 && ids_dtype != MAS_DTYPE_INT64) return MAS_ERR_UNSUPPORTED_DTYPE;
@@ -555,6 +616,7 @@ int mas_embedding_gather(void* out, const void* table, const void* ids, int ids_
   a.out = out; a.table = table; a.ids = ids; a.T = num_tokens; a.V = vocab_size;
   a.out_stride_b = out_stride * elem_size; a.table_stride_b = table_stride * elem_size;
   a.row_bytes = (uint32_t)row_bytes; a.status = status; a.fault = st->fault;
+  a.last = last; a.n_last = num_last; a.last_is_64 = last_dtype == MAS_DTYPE_INT64 ? 1 : 0;
   const bool i64 = ids_dtype == MAS_DTYPE_INT64;
   const bool tma = row_bytes % 16 == 0 && row_bytes <= 64 * 1024 && aligned(out, 16) &&
                    aligned(table, 16) && a.out_stride_b % 16 == 0 && a.table_stride_b % 16 == 0;
@@ -582,6 +644,26 @@ int mas_embedding_gather(void* out, const void* table, const void* ids, int ids_
   const dim3 grid((unsigned)std::min<int64_t>(ceil_div(num_tokens, 8), 1 << 20));
   if (i64) return launch(embed_generic_kernel<int64_t>, grid, dim3(256), 0, stream, enable_pdl, a, unit);
   return launch(embed_generic_kernel<int32_t>, grid, dim3(256), 0, stream, enable_pdl, a, unit);
+}
+
+int mas_embedding_gather(void* out, const void* table, const void* ids, int ids_dtype,
+                         int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
+                         int64_t out_stride, int64_t table_stride, int elem_size,
+                         int32_t* status, int enable_pdl, void* stream) {
+  return gather_impl(out, table, ids, ids_dtype, num_tokens, hidden_size, vocab_size, out_stride,
+                     table_stride, elem_size, status, enable_pdl, stream, nullptr, MAS_DTYPE_INT32, 0);
+}
+
+int mas_embedding_gather_fill_placeholders(void* out, const void* table, void* ids, int ids_dtype,
+                                           const void* last_tokens, int last_dtype, int64_t num_last,
+                                           int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
+                                           int64_t out_stride, int64_t table_stride, int elem_size,
+                                           int32_t* status, int enable_pdl, void* stream) {
+  if (last_dtype != MAS_DTYPE_INT32 && last_dtype != MAS_DTYPE_INT64) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (num_last < 0 || (num_last > 0 && last_tokens == nullptr)) return MAS_ERR_INVALID_ARGUMENT;
+  return gather_impl(out, table, ids, ids_dtype, num_tokens, hidden_size, vocab_size, out_stride,
+                     table_stride, elem_size, status, enable_pdl, stream,
+                     num_last > 0 ? last_tokens : nullptr, last_dtype, num_last);
 }
 
 }  // extern "C"

@@ -232,7 +232,9 @@ __host__ __device__ inline size_t norm_row_smem_bytes(int H, int rpc, int elem_b
   return (size_t)rpc * 2 * (size_t)H * (size_t)elem_bytes + 16 + (size_t)(kNormRowMaxThreads / 32) * sizeof(float);
 }
 
-template <typename T, bool QUANT>
+// MAXV bounds the 16-byte vectors a thread handles per row (ceil(H/8 / tpr)); the thread's weight
+// slice is loaded into registers before the row arrives, so its latency overlaps the bulk copies.
+template <typename T, bool QUANT, int MAXV>
 __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const NormArgs a, int tpr, int rpc) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = a.H;
@@ -264,6 +266,12 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
   }
   float inv_scale = 1.0f;
   if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
+  Vec16 wv[MAXV];
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = rt + j * tpr;
+    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+  }
   const bool ok = mbar_wait_bounded(bar, 0);
   const bool active = rr < nrows;
   const int64_t row = row0 + rr;
@@ -272,7 +280,10 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
 
   float ss = 0.f;
   if (ok && active) {
-    for (int v = rt; v < NV; v += tpr) {
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int v = rt + j * tpr;
+      if (v >= NV) break;
       float xf[8], rf[8];
       unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
       unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
@@ -296,11 +307,14 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
     const int w0 = (rr * tpr) >> 5, nw = tpr >> 5;
     for (int w = 0; w < nw; ++w) tot += red[w0 + w];
     const float rstd = rsqrtf(tot * (1.0f / (float)H) + a.eps);
-    for (int v = rt; v < NV; v += tpr) {
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int v = rt + j * tpr;
+      if (v >= NV) break;
       float xf[8], rf[8], wf[8];
       unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
       unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
-      unpack8<T>(ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8), wf);
+      unpack8<T>(wv[j], wf);
 #pragma unroll
       for (int e = 0; e < 8; ++e) xf[e] = (xf[e] + rf[e]) * rstd * wf[e];
       if constexpr (QUANT) {

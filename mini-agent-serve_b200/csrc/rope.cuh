@@ -31,6 +31,8 @@ struct RopeArgs {
   int32_t rd;    // rotary dim
   int32_t tpu;   // threads per unit, rd / 16 (vector path)
   int32_t* status;
+  float q_beta;      // llama-4 query scale (0: off), see llama4_q_scale
+  float q_inv_orig;  // fp32 reciprocal of original_max_position_embeddings
 };
 
 constexpr int kRopeThreads = 256;
@@ -51,6 +53,23 @@ __device__ __forceinline__ void load_f8(const float* p, float (&f)[8]) {
 __device__ __forceinline__ void rotate(float a, float b, float c, float s, float& ra, float& rb) {
   ra = __fmaf_rn(a, c, -__fmul_rn(b, s));
   rb = __fmaf_rn(b, c, __fmul_rn(a, s));
+}
+
+// llama-4 query scale of a token (Devstral2Attention.forward, devstral2.py:175-179), evaluated the
+// way eager torch evaluates `1 + beta * log1p(floor(pos.float() / original_max))` on CUDA: the
+// division by the host scalar is a multiplication by its fp32 reciprocal, every operation is rounded
+// separately (no contraction into an fma), and the result is rounded to the activation type before
+// it multiplies q.
+template <typename T>
+__device__ __forceinline__ float llama4_q_scale(int64_t pos, float beta, float inv_orig) {
+  const float k = floorf(__fmul_rn((float)pos, inv_orig));
+  return Elem<T>::to_f(Elem<T>::from_f(__fadd_rn(1.0f, __fmul_rn(beta, log1pf(k)))));
+}
+
+// The rotated q value as the reference holds it (rounded to T), times the token's scale.
+template <typename T>
+__device__ __forceinline__ float scaled_q(float rotated, float scale) {
+  return __fmul_rn(Elem<T>::to_f(Elem<T>::from_f(rotated)), scale);
 }
 
 // Each thread group handles kRopeUnits adjacent units per iteration (usually heads of one token,
@@ -77,7 +96,7 @@ __global__ void __launch_bounds__(kRopeThreads) rope_vec_kernel(const RopeArgs a
     const uint32_t stride = gridDim.x * (uint32_t)upb * kRopeUnits;
     for (uint32_t u0 = (blockIdx.x * (uint32_t)upb + (uint32_t)g) * kRopeUnits; u0 < units; u0 += stride) {
       T* ptr[kRopeUnits];
-      uint32_t tok[kRopeUnits];
+      uint32_t tok[kRopeUnits], head[kRopeUnits];
       Vec16 v0[kRopeUnits], v1[kRopeUnits];
 #pragma unroll
       for (int i = 0; i < kRopeUnits; ++i) {
@@ -87,6 +106,7 @@ __global__ void __launch_bounds__(kRopeThreads) rope_vec_kernel(const RopeArgs a
           const uint32_t t = u / NH;
           const uint32_t h = u - t * NH;
           tok[i] = t;
+          head[i] = h;
           ptr[i] = (h < (uint32_t)a.Hq)
                        ? static_cast<T*>(a.q) + (int64_t)t * a.qsn + (int64_t)h * a.qsh
                        : static_cast<T*>(a.k) + (int64_t)t * a.ksn + (int64_t)(h - a.Hq) * a.ksh;
@@ -118,6 +138,14 @@ __global__ void __launch_bounds__(kRopeThreads) rope_vec_kernel(const RopeArgs a
             rotate(x1[2 * e], x1[2 * e + 1], cs[4 + e], sn[4 + e], o1[2 * e], o1[2 * e + 1]);
           }
         }
+        if (a.q_beta != 0.f && head[i] < (uint32_t)a.Hq) {
+          const float qs = llama4_q_scale<T>(pos, a.q_beta, a.q_inv_orig);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            o0[e] = scaled_q<T>(o0[e], qs);
+            o1[e] = scaled_q<T>(o1[e], qs);
+          }
+        }
         st_plain(ptr[i] + off0, pack8<T>(o0));
         st_plain(ptr[i] + off1, pack8<T>(o1));
       }
@@ -147,6 +175,8 @@ struct RopeRingArgs {
   int32_t tokens_per_cta;
   int32_t* status;
   int32_t* fault;
+  float q_beta;      // llama-4 query scale (0: off), see llama4_q_scale
+  float q_inv_orig;
 };
 
 constexpr int kRopeConsumerWarps = 8;
@@ -233,6 +263,7 @@ __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeR
         const unsigned char* st = smem + (size_t)s * stage_bytes;
         const float* c = reinterpret_cast<const float*>(st + q_bytes + k_bytes);
         const int64_t t = tok0 + i;
+        const float qs = a.q_beta != 0.f ? llama4_q_scale<T>(spos[i], a.q_beta, a.q_inv_orig) : 0.f;
         for (int gi = ct; gi < groups; gi += ncons) {
           const int h = gi / tpu;
           const int j = gi - h * tpu;
@@ -261,6 +292,13 @@ __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeR
             for (int e = 0; e < 4; ++e) {
               rotate(x0[2 * e], x0[2 * e + 1], cs[e], sn[e], o0[2 * e], o0[2 * e + 1]);
               rotate(x1[2 * e], x1[2 * e + 1], cs[4 + e], sn[4 + e], o1[2 * e], o1[2 * e + 1]);
+            }
+          }
+          if (a.q_beta != 0.f && h < a.Hq) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              o0[e] = scaled_q<T>(o0[e], qs);
+              o1[e] = scaled_q<T>(o1[e], qs);
             }
           }
           st_plain(gh + off0, pack8<T>(o0));
@@ -302,8 +340,36 @@ __global__ void __launch_bounds__(kRopeThreads) rope_generic_kernel(const RopeAr
     const int64_t i1 = NEOX ? i + half : 2 * i + 1;
     float r0, r1;
     rotate(Elem<T>::to_f(p[i0]), Elem<T>::to_f(p[i1]), c, s, r0, r1);
+    if (a.q_beta != 0.f && h < a.Hq) {
+      const float qs = llama4_q_scale<T>(pos, a.q_beta, a.q_inv_orig);
+      r0 = scaled_q<T>(r0, qs);
+      r1 = scaled_q<T>(r1, qs);
+    }
     p[i0] = Elem<T>::from_f(r0);
     p[i1] = Elem<T>::from_f(r1);
+  }
+  pdl_launch_dependents();
+}
+
+// The llama-4 query scale of the elements past rotary_dim (partial rotary only): q[t, h, i] for
+// rotary_dim <= i < head_size, one element per thread. Tokens with an out-of-range position are
+// left as is, like the rotation.
+template <typename T, typename PosT>
+__global__ void __launch_bounds__(kRopeThreads) rope_q_tail_scale_kernel(const RopeArgs a, int32_t head_size) {
+  pdl_wait();
+  const int64_t tail = head_size - a.rd;
+  const int64_t total = a.T * a.Hq * tail;
+  const PosT* pos_p = static_cast<const PosT*>(a.pos);
+  for (int64_t idx = (int64_t)blockIdx.x * kRopeThreads + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * kRopeThreads) {
+    const int64_t i = a.rd + idx % tail;
+    const int64_t th = idx / tail;
+    const int64_t h = th % a.Hq;
+    const int64_t t = th / a.Hq;
+    const int64_t pos = (int64_t)pos_p[t];
+    if (pos < 0 || pos >= a.P) continue;
+    uint16_t* p = static_cast<uint16_t*>(a.q) + t * a.qsn + h * a.qsh + i;
+    *p = Elem<T>::from_f(__fmul_rn(Elem<T>::to_f(*p), llama4_q_scale<T>(pos, a.q_beta, a.q_inv_orig)));
   }
   pdl_launch_dependents();
 }

@@ -2,8 +2,8 @@
 // gate = in[t, i], up = in[t, d + i], silu(v) = v / (1 + exp(-v)) in fp32.
 //
 // Semantics follow flashinfer 0.6.11.post2 (FI/data/include/flashinfer/activation.cuh:29-65 with
-// the activation of FI/jit/activation.py:77-80, which uses the __expf intrinsic): fp32 math and
-// one rounding of the product.
+// the activation of FI/jit/activation.py:77-80, compiled with fast math: the __expf intrinsic and
+// the approximate divide): fp32 math and one rounding of the product.
 //
 // Pure streaming (6 bytes per output element, nothing reused), so the design is about bytes in
 // flight per SM without spending registers on them. Fast path: a persistent, warp-specialised TMA
@@ -32,7 +32,11 @@ struct SiluArgs {
   int32_t* fault;
 };
 
-__device__ __forceinline__ float silu_f32(float v) { return v / (1.0f + __expf(-v)); }
+// flashinfer compiles `val / (1.0f + __expf(-val))` with fast math, which makes the quotient the
+// approximate divide: the numerator times the reciprocal of the divisor, where a divisor of 2^126 or
+// more (gate below about -87.3) has a zero reciprocal. __fdividef is that divide, and it reproduces
+// the reference's outputs there (-0), not the tiny values an IEEE quotient would give.
+__device__ __forceinline__ float silu_f32(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
 constexpr int kSiluThreads = 256;            // scalar path
 constexpr int kSiluConsumerWarps = 16;
@@ -132,7 +136,7 @@ __host__ __device__ inline size_t silu_async_smem_bytes() {
 
 template <typename T>
 __global__ void __launch_bounds__(kSiluAsyncThreads) silu_mul_async_kernel(const SiluArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   pdl_wait();
   const int nvec = a.d >> 3;
   const int v = blockIdx.x * kSiluAsyncThreads + threadIdx.x;

@@ -109,6 +109,21 @@ void apply_rope_pos_ids_cos_sin_cache(at::Tensor q, at::Tensor k, at::Tensor cos
         "mas_rope_cos_sin_cache_inplace");
 }
 
+void apply_rope_q_scale(at::Tensor q, at::Tensor k, at::Tensor cos_sin_cache, at::Tensor pos_ids, bool interleave,
+                        double beta, int64_t original_max, bool enable_pdl, std::optional<at::Tensor> status) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3, "mas_b200: q and k must be (tokens, heads, head_size) views");
+  TORCH_CHECK(cos_sin_cache.dim() == 2 && cos_sin_cache.is_contiguous(), "mas_b200: cos_sin_cache must be contiguous");
+  TORCH_CHECK(q.size(2) == k.size(2), "mas_b200: q and k head sizes differ");
+  int32_t* st = status.has_value() ? status->data_ptr<int32_t>() : nullptr;
+  check(mas_rope_cos_sin_cache_q_scale_inplace(
+            pos_ids.data_ptr(), id_code(pos_ids), q.data_ptr(), k.data_ptr(), cos_sin_cache.data_ptr<float>(),
+            q.size(0), q.size(1), k.size(1), q.size(2), cos_sin_cache.size(1), cos_sin_cache.size(0), q.stride(0),
+            q.stride(1), k.stride(0), k.stride(1), interleave ? 0 : 1, static_cast<float>(beta), original_max,
+            act_code(q), st, enable_pdl, stream_of(q)),
+        "mas_rope_cos_sin_cache_q_scale_inplace");
+}
+
 void gather(at::Tensor& out, const at::Tensor& ids, const at::Tensor& weight, bool enable_pdl,
             const std::optional<at::Tensor>& status) {
   TORCH_CHECK(weight.dim() == 2 && weight.stride(1) == 1, "mas_b200: weight must be (num_embeddings, dim)");
@@ -130,6 +145,25 @@ at::Tensor embedding(at::Tensor input_ids, at::Tensor weight, bool enable_pdl, s
   return out;
 }
 
+at::Tensor embedding_fill(at::Tensor input_ids, at::Tensor weight, at::Tensor last_tokens, bool enable_pdl,
+                          std::optional<at::Tensor> status) {
+  const c10::cuda::CUDAGuard guard(weight.device());
+  TORCH_CHECK(weight.dim() == 2 && weight.stride(1) == 1, "mas_b200: weight must be (num_embeddings, dim)");
+  TORCH_CHECK(input_ids.is_contiguous(), "mas_b200: input_ids must be contiguous (it is updated in place)");
+  TORCH_CHECK(last_tokens.is_contiguous(), "mas_b200: last_tokens must be contiguous");
+  std::vector<int64_t> shape(input_ids.sizes().begin(), input_ids.sizes().end());
+  shape.push_back(weight.size(1));
+  at::Tensor out = at::empty(shape, weight.options());
+  int32_t* st = status.has_value() ? status->data_ptr<int32_t>() : nullptr;
+  check(mas_embedding_gather_fill_placeholders(
+            out.data_ptr(), weight.data_ptr(), input_ids.data_ptr(), id_code(input_ids), last_tokens.data_ptr(),
+            id_code(last_tokens), last_tokens.numel(), input_ids.numel(), weight.size(1), weight.size(0),
+            weight.size(1), weight.stride(0), static_cast<int>(weight.element_size()), st, enable_pdl,
+            stream_of(weight)),
+        "mas_embedding_gather_fill_placeholders");
+  return out;
+}
+
 void embedding_out(at::Tensor out, at::Tensor input_ids, at::Tensor weight, bool enable_pdl,
                    std::optional<at::Tensor> status) {
   const c10::cuda::CUDAGuard guard(weight.device());
@@ -145,8 +179,12 @@ TORCH_LIBRARY(mas_b200, m) {
   m.def("silu_and_mul(Tensor(a!) out, Tensor input, bool enable_pdl) -> ()");
   m.def("apply_rope_pos_ids_cos_sin_cache(Tensor(a!) q, Tensor(b!) k, Tensor cos_sin_cache, Tensor pos_ids, "
         "bool interleave, bool enable_pdl, Tensor(c!)? status) -> ()");
+  m.def("apply_rope_q_scale(Tensor(a!) q, Tensor(b!) k, Tensor cos_sin_cache, Tensor pos_ids, bool interleave, "
+        "float beta, int original_max, bool enable_pdl, Tensor(c!)? status) -> ()");
   m.def("embedding(Tensor input_ids, Tensor weight, bool enable_pdl, Tensor(a!)? status) -> Tensor");
   m.def("embedding_out(Tensor(a!) out, Tensor input_ids, Tensor weight, bool enable_pdl, Tensor(b!)? status) -> ()");
+  m.def("embedding_fill(Tensor(a!) input_ids, Tensor weight, Tensor last_tokens, bool enable_pdl, "
+        "Tensor(b!)? status) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(mas_b200, CUDA, m) {
@@ -154,6 +192,8 @@ TORCH_LIBRARY_IMPL(mas_b200, CUDA, m) {
   m.impl("fused_add_rmsnorm_quant", &fused_add_rmsnorm_quant);
   m.impl("silu_and_mul", &silu_and_mul);
   m.impl("apply_rope_pos_ids_cos_sin_cache", &apply_rope_pos_ids_cos_sin_cache);
+  m.impl("apply_rope_q_scale", &apply_rope_q_scale);
   m.impl("embedding", &embedding);
   m.impl("embedding_out", &embedding_out);
+  m.impl("embedding_fill", &embedding_fill);
 }

@@ -34,8 +34,10 @@ __all__ = [
     "fused_add_rmsnorm_quant",
     "silu_and_mul",
     "apply_rope_with_cos_sin_cache_inplace",
+    "apply_rope_and_llama4_query_scale_inplace",
     "embedding",
     "embedding_out",
+    "embedding_fill_placeholders",
     "status_word",
     "read_status",
 ]
@@ -108,8 +110,10 @@ _OP_NORM = torch.ops.mas_b200.fused_add_rmsnorm.default
 _OP_NORM_QUANT = torch.ops.mas_b200.fused_add_rmsnorm_quant.default
 _OP_SILU = torch.ops.mas_b200.silu_and_mul.default
 _OP_ROPE = torch.ops.mas_b200.apply_rope_pos_ids_cos_sin_cache.default
+_OP_ROPE_QS = torch.ops.mas_b200.apply_rope_q_scale.default
 _OP_EMBED = torch.ops.mas_b200.embedding.default
 _OP_EMBED_OUT = torch.ops.mas_b200.embedding_out.default
+_OP_EMBED_FILL = torch.ops.mas_b200.embedding_fill.default
 
 
 def _check_norm(input: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor) -> None:
@@ -251,6 +255,49 @@ def apply_rope_with_cos_sin_cache_inplace(positions: torch.Tensor, query: torch.
              _status_arg(query.device))
 
 
+@torch.library.register_fake("mas_b200::apply_rope_q_scale")
+def _(q, k, cos_sin_cache, pos_ids, interleave, beta, original_max, enable_pdl, status) -> None:
+    return None
+
+
+def apply_rope_and_llama4_query_scale_inplace(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
+                                              head_size: int, cos_sin_cache: torch.Tensor, beta: float,
+                                              original_max_position_embeddings: int, is_neox: bool = True,
+                                              enable_pdl: Optional[bool] = None) -> None:
+    r"""Rotary embedding of q and k fused with Devstral 2's llama-4 query scale, in place.
+
+    Equivalent to the two steps of Devstral2Attention.forward (devstral2.py:163-166 and :175-179)::
+
+        apply_rope_with_cos_sin_cache_inplace(positions, query, key, head_size, cos_sin_cache, is_neox)
+        scale = 1 + beta * torch.log1p(torch.floor(positions.float() / original_max_position_embeddings))
+        query *= scale[:, None].to(query.dtype)
+
+    with the difference that q is scaled in place instead of into a new tensor (the reference does not
+    use the unscaled q afterwards). One pass over q instead of three (rope, scale, multiply).
+    """
+    if original_max_position_embeddings <= 0:
+        raise ValueError("original_max_position_embeddings must be positive")
+    if cos_sin_cache.dtype != torch.float32:
+        raise ValueError("cos_sin_cache should be float32")
+    if cos_sin_cache.dim() != 2 or not cos_sin_cache.is_contiguous():
+        raise ValueError("cos_sin_cache must be a contiguous (max_seq_len, rotary_dim) tensor")
+    if positions.dtype not in _ID_DTYPES:
+        raise ValueError(f"positions must be int32 or int64, got {positions.dtype}")
+    if query.dtype != key.dtype:
+        raise ValueError("query and key must share one dtype")
+    rotary_dim = cos_sin_cache.shape[1]
+    if rotary_dim % 2 != 0 or rotary_dim > head_size:
+        raise ValueError(f"rotary_dim {rotary_dim} must be even and <= head_size {head_size}")
+    if query.shape[0] != positions.shape[0] or key.shape[0] != positions.shape[0]:
+        raise ValueError("positions, query and key must have the same number of tokens")
+    if positions.shape[0] == 0:
+        return
+    q = query.view(query.shape[0], -1, head_size)
+    k = key.view(key.shape[0], -1, head_size)
+    _OP_ROPE_QS(q, k, cos_sin_cache, positions, not is_neox, float(beta), int(original_max_position_embeddings),
+                True if enable_pdl is None else bool(enable_pdl), _status_arg(query.device))
+
+
 # ------------------------------------------------------------------------------------------------
 # Token-embedding gather.
 # ------------------------------------------------------------------------------------------------
@@ -292,3 +339,31 @@ def embedding_out(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tens
     _OP_EMBED_OUT(out, input_ids.contiguous(), weight, True if enable_pdl is None else bool(enable_pdl),
                   _status_arg(weight.device))
     return out
+
+
+@torch.library.register_fake("mas_b200::embedding_fill")
+def _(input_ids, weight, last_tokens, enable_pdl, status):
+    return weight.new_empty(tuple(input_ids.shape) + (weight.shape[1],))
+
+
+def embedding_fill_placeholders(input_ids: torch.Tensor, weight: torch.Tensor, last_tokens: torch.Tensor,
+                                enable_pdl: Optional[bool] = None) -> torch.Tensor:
+    """ModelRunner.fill_placeholders then the embedding gather, in one launch.
+
+    Equivalent to (miniagentserve/engine/model_runner.py:149-154, then devstral2.py:282)::
+
+        is_placeholder = input_ids < 0
+        rows = (-1 - input_ids).clamp(min=0)
+        input_ids.copy_(torch.where(is_placeholder, last_tokens[rows], input_ids))
+        return embed_tokens(input_ids)
+
+    `input_ids` is updated in place. A placeholder naming a row past the end of `last_tokens` gives a
+    zero row and sets MAS_STATUS_EMBED_ID_OUT_OF_RANGE (torch would raise a device-side assert).
+    """
+    _check_embedding(input_ids, weight)
+    if last_tokens.dtype not in _ID_DTYPES:
+        raise ValueError(f"last_tokens must be int32 or int64, got {last_tokens.dtype}")
+    if not input_ids.is_contiguous():
+        raise ValueError("input_ids must be contiguous (it is updated in place)")
+    return _OP_EMBED_FILL(input_ids, weight, last_tokens.contiguous(),
+                          True if enable_pdl is None else bool(enable_pdl), _status_arg(weight.device))

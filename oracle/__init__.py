@@ -60,7 +60,12 @@ _SIGS = {
     "orc_silu_and_mul": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i32]),
     "orc_rope_cos_sin_cache_inplace": (
         _i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
+    "orc_rope_cos_sin_cache_q_scale_inplace": (
+        _i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _f32, _i64,
+               _i32, _vp]),
     "orc_embedding_gather": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
+    "orc_embedding_gather_fill_placeholders": (
+        _i32, [_vp, _vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
     "orc_f32_to_e4m3": (ctypes.c_uint8, [_f32]),
     "orc_e4m3_to_f32": (_f32, [ctypes.c_uint8]),
     "orc_f32_to_bf16": (ctypes.c_uint16, [_f32]),
@@ -152,6 +157,24 @@ def apply_rope_with_cos_sin_cache_inplace(positions: torch.Tensor, query: torch.
     return st.value
 
 
+def apply_rope_and_llama4_query_scale_inplace(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
+                                              head_size: int, cos_sin_cache: torch.Tensor, beta: float,
+                                              original_max_position_embeddings: int, is_neox: bool = True) -> int:
+    """Rope then the llama-4 query scale, in place on CPU q/k; returns the status bits."""
+    for n, t in (("positions", positions), ("query", query), ("key", key), ("cos_sin_cache", cos_sin_cache)):
+        _cpu(t, n)
+    cache = cos_sin_cache.contiguous()
+    q = query.view(query.shape[0], -1, head_size)
+    k = key.view(key.shape[0], -1, head_size)
+    st = ctypes.c_int32(0)
+    _ok(lib().orc_rope_cos_sin_cache_q_scale_inplace(
+        positions.data_ptr(), _IDS[positions.dtype], q.data_ptr(), k.data_ptr(), cache.data_ptr(), q.shape[0],
+        q.shape[1], k.shape[1], head_size, cache.shape[1], cache.shape[0], q.stride(0), q.stride(1), k.stride(0),
+        k.stride(1), int(bool(is_neox)), float(beta), int(original_max_position_embeddings), _ACT[q.dtype],
+        ctypes.byref(st)), "rope_q_scale")
+    return st.value
+
+
 def embedding(input_ids: torch.Tensor, weight: torch.Tensor) -> tuple[torch.Tensor, int]:
     """(weight[input_ids] with zero rows for out-of-range ids, status bits (1 = an id out of range))."""
     _cpu(input_ids, "input_ids")
@@ -162,6 +185,21 @@ def embedding(input_ids: torch.Tensor, weight: torch.Tensor) -> tuple[torch.Tens
     _ok(lib().orc_embedding_gather(out.data_ptr(), weight.data_ptr(), ids.data_ptr(), _IDS[ids.dtype], ids.shape[0],
                                    weight.shape[1], weight.shape[0], weight.shape[1], weight.stride(0),
                                    weight.element_size(), ctypes.byref(st)), "embedding")
+    return out, st.value
+
+
+def embedding_fill_placeholders(input_ids: torch.Tensor, weight: torch.Tensor,
+                                last_tokens: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """fill_placeholders (in place on CPU input_ids) then the gather; returns (rows, status bits)."""
+    for n, t in (("input_ids", input_ids), ("weight", weight), ("last_tokens", last_tokens)):
+        _cpu(t, n)
+    assert input_ids.is_contiguous() and last_tokens.is_contiguous()
+    out = torch.empty(tuple(input_ids.shape) + (weight.shape[1],), dtype=weight.dtype)
+    st = ctypes.c_int32(0)
+    _ok(lib().orc_embedding_gather_fill_placeholders(
+        out.data_ptr(), weight.data_ptr(), input_ids.data_ptr(), _IDS[input_ids.dtype], last_tokens.data_ptr(),
+        _IDS[last_tokens.dtype], last_tokens.numel(), input_ids.numel(), weight.shape[1], weight.shape[0],
+        weight.shape[1], weight.stride(0), weight.element_size(), ctypes.byref(st)), "embedding_fill")
     return out, st.value
 
 

@@ -53,6 +53,7 @@ static inline float f16_to_f32(uint16_t h) { _Float16 v; memcpy(&v, &h, 2); retu
 static inline uint16_t f32_to_f16(float f) { _Float16 v = (_Float16)f; uint16_t h; memcpy(&h, &v, 2); return h; }
 
 static inline float ld_act(const uint16_t* p, int dtype) { return dtype == ORC_BF16 ? bf16_to_f32(*p) : f16_to_f32(*p); }
+static inline float ld_act_from(uint16_t h, int dtype) { return dtype == ORC_BF16 ? bf16_to_f32(h) : f16_to_f32(h); }
 static inline uint16_t to_act(float f, int dtype) { return dtype == ORC_BF16 ? f32_to_bf16(f) : f32_to_f16(f); }
 
 /* binary32 -> float8 e4m3fn (bias 7, no infinities, max finite 448 = 0x7e, NaN = 0x7f), round to
@@ -166,8 +167,10 @@ int orc_fused_add_rmsnorm_quant(void* out, const void* input, void* residual, co
 /* ---------------------------------------------------------------------------------------------
  * SiLU and mul. FI/data/include/flashinfer/activation.cuh:43-49 with FI/jit/activation.py:77-80:
  *   out = round(silu(g) * u),  silu(g) = g / (1 + exp(-g)),  all fp32.
- * exp is evaluated in double and rounded to fp32 (so it overflows to +inf exactly where the fp32
- * exponential does, g < about -88.72, giving silu = -0 there like the GPU).
+ * exp is evaluated in double and rounded to fp32. flashinfer compiles the quotient with fast math
+ * (the approximate divide, g times the reciprocal of the divisor), whose reciprocal is 0 for a
+ * divisor of 2^126 or more: silu is then g * 0 (= -0 for the negative g concerned), which the
+ * B200 fixtures confirm (gate below about -87.3). Elsewhere the exact quotient is used.
  * --------------------------------------------------------------------------------------------- */
 int orc_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
                      int64_t out_stride, int64_t input_stride, int dtype) {
@@ -180,7 +183,8 @@ int orc_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
     for (int64_t i = 0; i < d; ++i) {
       const float gv = ld_act(&g[i], dtype);
       const float e = (float)exp(-(double)gv);
-      const float s = gv / (1.0f + e);
+      const float den = 1.0f + e;
+      const float s = den >= 0x1p126f ? gv * 0.0f : gv / den;
       o[i] = to_act(s * ld_act(&u[i], dtype), dtype);
     }
   }
@@ -233,6 +237,47 @@ int orc_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, v
 }
 
 /* ---------------------------------------------------------------------------------------------
+ * Rotary embedding followed by the llama-4 query scale of Devstral2Attention.forward
+ * (miniagentserve/models/devstral2/devstral2.py:163-166 then :175-179), as eager torch evaluates it on
+ * CUDA: scale = to_act(1 + beta * log1p(floor(pos_f32 * (1 / original_max)))), each fp32 step rounded
+ * on its own (`tensor / host_scalar` is a multiplication by the fp32 reciprocal there); every q
+ * element (rotated or not) becomes to_act(to_act(q) * scale). k is rotated only.
+ * --------------------------------------------------------------------------------------------- */
+static inline float llama4_q_scale(int64_t pos, float beta, float inv_orig, int dtype) {
+  const float k = floorf((float)pos * inv_orig);
+  const float s = 1.0f + beta * log1pf(k);
+  return ld_act_from(to_act(s, dtype), dtype);
+}
+
+int orc_rope_cos_sin_cache_q_scale_inplace(const void* positions, int positions_dtype, void* query,
+                                           void* key, const float* cache, int64_t num_tokens,
+                                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                                           int64_t rotary_dim, int64_t max_positions,
+                                           int64_t q_stride_token, int64_t q_stride_head,
+                                           int64_t k_stride_token, int64_t k_stride_head, int is_neox,
+                                           float beta, int64_t original_max, int dtype, int32_t* status) {
+  if (original_max <= 0) return -1;
+  const int rc = orc_rope_cos_sin_cache_inplace(positions, positions_dtype, query, key, cache, num_tokens,
+                                                num_q_heads, num_kv_heads, head_size, rotary_dim,
+                                                max_positions, q_stride_token, q_stride_head,
+                                                k_stride_token, k_stride_head, is_neox, dtype, status);
+  if (rc != 0 || beta == 0.0f) return rc;
+  const float inv_orig = 1.0f / (float)original_max;
+#pragma omp parallel for schedule(static)
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    const int64_t pos = positions_dtype == ORC_INT64 ? ((const int64_t*)positions)[t]
+                                                     : (int64_t)((const int32_t*)positions)[t];
+    if (pos < 0 || pos >= max_positions) continue;
+    const float sc = llama4_q_scale(pos, beta, inv_orig, dtype);
+    for (int64_t h = 0; h < num_q_heads; ++h) {
+      uint16_t* p = (uint16_t*)query + t * q_stride_token + h * q_stride_head;
+      for (int64_t i = 0; i < head_size; ++i) p[i] = to_act(ld_act(&p[i], dtype) * sc, dtype);
+    }
+  }
+  return 0;
+}
+
+/* ---------------------------------------------------------------------------------------------
  * Token-embedding gather: out[t] = table[ids[t]], a byte copy (torch.nn.functional.embedding).
  * Out-of-range ids give a zero row and set bit 1 of *status.
  * --------------------------------------------------------------------------------------------- */
@@ -252,4 +297,23 @@ int orc_embedding_gather(void* out, const void* table, const void* ids, int ids_
   }
   if (status) *status |= flags;
   return 0;
+}
+
+/* ModelRunner.fill_placeholders (miniagentserve/engine/model_runner.py:149-154) then the gather: an id
+ * -1-r (r >= 0) is replaced, in `ids`, by last[r]; r >= n_last is an out-of-range id. */
+int orc_embedding_gather_fill_placeholders(void* out, const void* table, void* ids, int ids_dtype,
+                                           const void* last, int last_dtype, int64_t n_last,
+                                           int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
+                                           int64_t out_stride, int64_t table_stride, int elem_size,
+                                           int32_t* status) {
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    int64_t id = ids_dtype == ORC_INT64 ? ((int64_t*)ids)[t] : (int64_t)((int32_t*)ids)[t];
+    if (id >= 0) continue;
+    const int64_t r = -1 - id;
+    if (r >= n_last) continue; /* stays negative: gathered as out of range */
+    id = last_dtype == ORC_INT64 ? ((const int64_t*)last)[r] : (int64_t)((const int32_t*)last)[r];
+    if (ids_dtype == ORC_INT64) ((int64_t*)ids)[t] = id; else ((int32_t*)ids)[t] = (int32_t)id;
+  }
+  return orc_embedding_gather(out, table, ids, ids_dtype, num_tokens, hidden_size, vocab_size, out_stride,
+                              table_stride, elem_size, status);
 }

@@ -29,7 +29,9 @@ def torch_silu(x):
     d = x.shape[-1] // 2
     g, u = x[..., :d].float(), x[..., d:].float()
     e = torch.exp(-g.double()).float()
-    return (g / (1.0 + e) * u).to(x.dtype)
+    den = 1.0 + e
+    s = torch.where(den >= 2.0 ** 126, g * 0.0, g / den)  # the approximate divide's zero reciprocal
+    return (s * u).to(x.dtype)
 
 
 def torch_rope(pos, q, k, D, cache, neox=True):
@@ -139,3 +141,48 @@ def test_embedding_out_of_range_and_dtypes():
     assert torch.count_nonzero(out[1, 1]) == 0
     out32, st32 = oracle.embedding(ids[0].to(torch.int32), table.to(torch.bfloat16))
     assert st32 == 0 and torch.equal(out32, table.to(torch.bfloat16)[ids[0]])
+
+
+@pytest.mark.parametrize("neox,orig,beta", [(True, 8192, 0.1), (False, 4096, 0.25), (True, 16384, 1.0)])
+def test_rope_llama4_query_scale_matches_reference_expression(neox, orig, beta):
+    """The fused rope + query scale against the reference's own torch expression (devstral2.py:175-179)
+    applied to the rotated q; original_max is a power of two, so `/` and `* (1/x)` agree exactly."""
+    g = torch.Generator().manual_seed(orig)
+    T, Hq, Hkv, D, P = 11, 3, 2, 64, 200000
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, generator=g).to(torch.bfloat16)
+    ang = torch.rand(P, D // 2, generator=g) * 6.28
+    cache = torch.cat([ang.cos(), ang.sin()], -1)
+    pos = torch.randint(0, P, (T,), generator=g).to(torch.int32)
+    pos[0], pos[1], pos[2] = 0, orig - 1, orig  # scale 1, 1, 1 + beta*log(2)
+    q, k = qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + Hkv) * D]
+    qt, kt = torch_rope(pos, q, k, D, cache, neox)
+    attn_scale = 1 + beta * torch.log1p(torch.floor(pos.float() / orig))
+    q_ref = qt.view(T, Hq, D) * attn_scale[:, None, None].to(torch.bfloat16)
+    qo = qkv.clone()
+    st = oracle.apply_rope_and_llama4_query_scale_inplace(pos, qo[:, : Hq * D], qo[:, Hq * D: (Hq + Hkv) * D], D,
+                                                          cache, beta, orig, is_neox=neox)
+    assert st == 0
+    assert_ulp(qo[:, : Hq * D], q_ref.reshape(T, -1), what="scaled q")
+    assert_ulp(qo[:, Hq * D: (Hq + Hkv) * D], kt, what="k (rotated only)")
+
+
+def test_embedding_fill_placeholders_matches_reference_expression():
+    """The oracle's fused fill + gather against ModelRunner.fill_placeholders' own torch expression
+    (model_runner.py:149-154) followed by the embedding."""
+    g = torch.Generator().manual_seed(9)
+    V, H = 300, 24
+    table = torch.randn(V, H, generator=g).to(torch.bfloat16)
+    last_tokens = torch.randint(0, V, (5,), generator=g, dtype=torch.int32)
+    ids = torch.tensor([7, -1, 299, -5, 0, -3, 12], dtype=torch.int64)
+    ref_ids = ids.clone()
+    rows = (-1 - ref_ids).clamp(min=0)
+    ref_ids.copy_(torch.where(ref_ids < 0, last_tokens[rows], ref_ids))
+    ref = table[ref_ids]
+    mine_ids = ids.clone()
+    out, st = oracle.embedding_fill_placeholders(mine_ids, table, last_tokens)
+    assert st == 0
+    assert torch.equal(mine_ids, ref_ids)
+    assert_bits_equal(out, ref, "rows")
+    bad = torch.tensor([-6, 3], dtype=torch.int64)  # row 5 of a 5-entry last_tokens
+    out, st = oracle.embedding_fill_placeholders(bad, table, last_tokens)
+    assert st == 1 and torch.count_nonzero(out[0].float()) == 0 and int(bad[0]) == -6
