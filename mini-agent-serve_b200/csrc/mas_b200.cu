@@ -88,8 +88,6 @@ cudaError_t prepare_current(DeviceState& st, int device) {
   if ((e = opt_in_norm_row<__nv_bfloat16, true>()) != cudaSuccess) return e;
   if ((e = opt_in_norm_row<__half, false>()) != cudaSuccess) return e;
   if ((e = opt_in_norm_row<__half, true>()) != cudaSuccess) return e;
-  if ((e = opt_in_smem(silu_mul_async_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(silu_mul_async_kernel<__half>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__half>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int32_t, true>)) != cudaSuccess) return e;
@@ -396,26 +394,11 @@ int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
   a.out_stride = out_stride; a.d = (int32_t)d; a.fault = st->fault;
   const bool vec = d % 8 == 0 && aligned(out, 16) && aligned(input, 16) && input_stride % 8 == 0 &&
                    out_stride % 8 == 0;
-  static const bool use_vec = env_is("MAS_SILU_IMPL", "vec");
   static const bool use_ring = env_is("MAS_SILU_IMPL", "ring");
-  if (vec && !use_vec && !use_ring) {
-    // Per-thread cp.async pipeline: column blocks of 256 vectors x row groups, every CTA resident.
-    const void* fn = dtype == MAS_DTYPE_BF16 ? (const void*)silu_mul_async_kernel<__nv_bfloat16>
-                                             : (const void*)silu_mul_async_kernel<__half>;
-    const size_t smem = silu_async_smem_bytes();
-    const int ctas = resident_ctas(fn, kSiluAsyncThreads, smem);
-    const int64_t gx = ceil_div(d / 8, kSiluAsyncThreads);
-    int64_t gy = std::min<int64_t>(num_tokens, 65535);
-    gy = std::max<int64_t>(1, std::min<int64_t>(gy, (int64_t)st->sm_count * ctas / std::max<int64_t>(1, gx)));
-    if (dtype == MAS_DTYPE_BF16)
-      return launch(silu_mul_async_kernel<__nv_bfloat16>, dim3((unsigned)gx, (unsigned)gy), dim3(kSiluAsyncThreads),
-                    smem, stream, enable_pdl, a);
-    return launch(silu_mul_async_kernel<__half>, dim3((unsigned)gx, (unsigned)gy), dim3(kSiluAsyncThreads), smem,
-                  stream, enable_pdl, a);
-  }
-  if (vec && use_vec) {
+  if (vec && !use_ring) {
+    static const int env_rows = env_int("MAS_SILU_GRID_ROWS", 0);
     const unsigned gx = (unsigned)ceil_div(d / 8, kSiluThreads);
-    const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, 65535);
+    const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, env_rows > 0 ? env_rows : 65535);
     if (dtype == MAS_DTYPE_BF16)
       return launch(silu_mul_vec_kernel<__nv_bfloat16>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
     return launch(silu_mul_vec_kernel<__half>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);

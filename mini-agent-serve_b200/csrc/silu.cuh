@@ -6,7 +6,8 @@
 // the approximate divide): fp32 math and one rounding of the product.
 //
 // Pure streaming (6 bytes per output element, nothing reused), so the design is about bytes in
-// flight per SM without spending registers on them. Fast path: a persistent, warp-specialised TMA
+// flight per SM. The default fast path is the register variant below (full occupancy at 32
+// registers). The alternative fast path (MAS_SILU_IMPL=ring) is a persistent, warp-specialised TMA
 // ring. The work is cut into tiles of (token, kSiluChunk columns); each CTA owns a contiguous range
 // of tiles. Warp 0 is the producer: one lane streams the gate and up halves of each tile into an
 // S-stage shared-memory ring with two bulk copies (cp.async.bulk, completion on the stage's `full`
@@ -123,63 +124,11 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
   pdl_launch_dependents();
 }
 
-// Per-thread pipeline variant: each thread owns one 16-byte column position and walks the rows
-// assigned to its CTA (row stride = gridDim.y), keeping kSiluAsyncDepth gate/up pairs in flight
-// through cp.async into its own shared-memory slots. No registers hold in-flight data and no warp
-// waits on another, so three 256-thread CTAs per SM keep ~190 KB of loads in flight.
-constexpr int kSiluAsyncThreads = 256;
-constexpr int kSiluAsyncDepth = 8;
-
-__host__ __device__ inline size_t silu_async_smem_bytes() {
-  return (size_t)kSiluAsyncDepth * kSiluAsyncThreads * 2 * 16;
-}
-
+// Register variant (the default fast path): one 16-byte gate/up pair per thread and row, 32
+// registers, so 2048 threads per SM keep 64 KB of loads in flight; a 2-D grid of (256-vector column
+// blocks, row groups), each thread walking the rows of its group.
 template <typename T>
-__global__ void __launch_bounds__(kSiluAsyncThreads) silu_mul_async_kernel(const SiluArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  pdl_wait();
-  const int nvec = a.d >> 3;
-  const int v = blockIdx.x * kSiluAsyncThreads + threadIdx.x;
-  if (v < nvec) {
-    const int64_t r0 = blockIdx.y, rs = gridDim.y;
-    const int n = (int)((a.rows - r0 + rs - 1) / rs);
-    Vec16* slots = reinterpret_cast<Vec16*>(smem) + threadIdx.x * 2;  // slot i: slots + i*2*threads
-    const T* in = static_cast<const T*>(a.in) + (size_t)v * 8;
-    T* out = static_cast<T*>(a.out) + (size_t)v * 8;
-    auto issue = [&](int i) {
-      const T* g = in + (r0 + (int64_t)i * rs) * a.in_stride;
-      Vec16* dst = slots + (size_t)(i % kSiluAsyncDepth) * 2 * kSiluAsyncThreads;
-      cp_async16(dst, g);
-      cp_async16(dst + 1, g + a.d);
-    };
-#pragma unroll 1
-    for (int i = 0; i < kSiluAsyncDepth; ++i) {
-      if (i < n) issue(i);
-      cp_async_commit();
-    }
-#pragma unroll 1
-    for (int i = 0; i < n; ++i) {
-      cp_async_wait<kSiluAsyncDepth - 1>();  // item i has landed
-      const Vec16* src = slots + (size_t)(i % kSiluAsyncDepth) * 2 * kSiluAsyncThreads;
-      const Vec16 gv = src[0], uv = src[1];
-      if (i + kSiluAsyncDepth < n) issue(i + kSiluAsyncDepth);  // refill the slot just read
-      cp_async_commit();
-      float gf[8], uf[8], y[8];
-      unpack8<T>(gv, gf);
-      unpack8<T>(uv, uf);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = silu_f32(gf[e]) * uf[e];
-      st_plain(out + (r0 + (int64_t)i * rs) * a.out_stride, pack8<T>(y));
-    }
-    cp_async_wait<0>();
-  }
-  pdl_launch_dependents();
-}
-
-// Register variant: one 16-byte gate/up pair per thread (at most 42 registers, so 1536 threads per
-// SM keep 48 KB of loads in flight), a 2-D grid of (256-vector column blocks, rows).
-template <typename T>
-__global__ void __launch_bounds__(kSiluThreads, 6) silu_mul_vec_kernel(const SiluArgs a) {
+__global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const SiluArgs a) {
   pdl_wait();
   const int nvec = a.d >> 3;
   const int v = blockIdx.x * kSiluThreads + threadIdx.x;

@@ -95,6 +95,24 @@ def main(out_dir: Path) -> None:
         out = silu_and_mul(xin.to(dev), enable_pdl=True)
         torch.cuda.synchronize()
         arrays.update({"silu_sneg_in": bits(xin), "silu_sneg_out": bits(out)})
+        # The silu output quantised for down_proj: FP8Linear.forward's quantize_fp8, the expression
+        # `(x / scale).clamp(-FP8_MAX, FP8_MAX).to(FP8)` under torch.compile(dynamic=True)
+        # (devstral2.py:93-95, :110-111), on flashinfer's silu output.
+        fp8 = torch.float8_e4m3fn
+        fp8_max = torch.finfo(fp8).max
+
+        @torch.compile(dynamic=True)
+        def quantize_fp8(x, scale):
+            return (x / scale).clamp(-fp8_max, fp8_max).to(fp8)
+
+        for name, T, d, sc in (("qs1", 8, 4096, 0.05), ("qs2", 3, 28672, 0.0137), ("qs3", 2, 1024, 1.7)):
+            xin = rnd(T, 2 * d, scale=3.0)
+            act = silu_and_mul(xin.to(dev), enable_pdl=True)
+            scale = torch.tensor(sc, dtype=torch.float32, device=dev)
+            q = quantize_fp8(act, scale)
+            torch.cuda.synchronize()
+            arrays.update({f"siluq_{name}_in": bits(xin), f"siluq_{name}_act": bits(act), f"siluq_{name}_out": bits(q),
+                           f"siluq_{name}_scale": np.array(sc, dtype=np.float32)})
     except Exception:
         failures.append("silu_and_mul: " + traceback.format_exc(limit=2))
 
