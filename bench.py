@@ -202,6 +202,23 @@ class FlashinferOps:
     def embedding_out(out, ids, table):
         return torch.index_select(table, 0, ids, out=out.view(-1, table.shape[1]))
 
+    _quantize = None
+
+    def silu_and_mul_quant(self, x, scale, out=None, enable_pdl=True):
+        """The reference's unfused pair: flashinfer silu_and_mul, then FP8Linear's compiled
+        quantize_fp8 (devstral2.py:93-95, :110-111)."""
+        if FlashinferOps._quantize is None:
+            fp8 = torch.float8_e4m3fn
+            fp8_max = torch.finfo(fp8).max
+
+            @torch.compile(dynamic=True)
+            def quantize_fp8(a, s):
+                return (a / s).clamp(-fp8_max, fp8_max).to(fp8)
+
+            FlashinferOps._quantize = quantize_fp8
+        # `out` is ignored: the reference allocates the quantised activation (no extra copy timed)
+        return FlashinferOps._quantize(self.silu_and_mul(x, enable_pdl=enable_pdl), scale)
+
 
 # --------------------------------------------------------------------------------------------------
 # Workloads: each builds device state and returns closures for one step.
@@ -326,15 +343,21 @@ class OpWorkload:
                         "tokens": self.T, "hidden": H, "l2": "inputs larger than L2"}
             if name == "norm_chain":
                 self.name = "norm"
-        elif name in ("silu", "silu_chain"):
-            self.x = (wl.silu_inputs(device, seed=4, tokens=4352, d=cs.intermediate_size) if name == "silu_chain"
+        elif name in ("silu", "silu_chain", "silu_fp8", "silu_fp8_chain"):
+            chain = name.endswith("_chain")
+            quant = name.startswith("silu_fp8")
+            self.x = (wl.silu_inputs(device, seed=4, tokens=4352, d=cs.intermediate_size) if chain
                       else wl.silu_inputs(device))
             self.T = self.x.shape[0]
-            self.out = torch.empty(self.T, self.x.shape[1] // 2, dtype=self.x.dtype, device=device)
-            self.bytes = 6 * self.T * self.out.shape[1]
-            self.cfg = {"workload": f"{'chain-shape' if name == 'silu_chain' else 'config 2'} SiLU-mul",
+            self.out = torch.empty(self.T, self.x.shape[1] // 2,
+                                   dtype=torch.float8_e4m3fn if quant else self.x.dtype, device=device)
+            self.scale = torch.tensor(0.0137, device=device)
+            # read gate + up (4 B), write the activation (2 B) or its e4m3 byte (1 B)
+            self.bytes = (5 if quant else 6) * self.T * self.out.shape[1]
+            self.cfg = {"workload": f"{'chain-shape' if chain else 'config 2'} SiLU-mul"
+                                    f"{' + fp8 activation quant' if quant else ''}",
                         "tokens": self.T, "d": self.out.shape[1], "l2": "inputs larger than L2"}
-            self.name = "silu"
+            self.name = "silu_fp8" if quant else "silu"
         elif name == "rope_chain":
             ids, pos = wl.chain_host_inputs()
             b = wl.chain_buffers(ids, pos, device=device, layers=1)
@@ -384,6 +407,8 @@ class OpWorkload:
             o.fused_add_rmsnorm_quant(self.out, self.x, self.r, self.w, self.scale, self.eps, enable_pdl=True)
         elif n == "silu":
             o.silu_and_mul(self.x, out=self.out, enable_pdl=True)
+        elif n == "silu_fp8":
+            o.silu_and_mul_quant(self.x, self.scale, out=self.out, enable_pdl=True)
         elif n == "rope":
             o.apply_rope_with_cos_sin_cache_inplace(self.pos, self.q, self.k, 128, self.cache, is_neox=True)
         elif n == "embed":
@@ -627,7 +652,7 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["mas", "reference", "flashinfer"], default="mas")
     ap.add_argument("--workload", choices=["chain", "norm", "norm_fp8", "silu", "rope", "embed", "norm_chain",
-                                           "silu_chain", "rope_chain"], default="chain")
+                                           "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain"], default="chain")
     ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

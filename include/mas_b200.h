@@ -109,6 +109,19 @@ MAS_API int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, i
                      void* stream);
 
 /*
+ * SiLU-and-mul fused with the activation quantisation of the down projection that consumes it:
+ *   act = round(silu(gate) * up) as mas_silu_and_mul stores it;
+ *   out[t * out_stride + i] = e4m3_rn(clamp(f32(act) / scale[0], -448, 448))   (IEEE quotient)
+ * Replaces the pair silu_and_mul (miniagentserve/models/devstral2/devstral2.py:224) ->
+ * FP8Linear.forward's quantize_fp8(x, activation_scale) (devstral2.py:93-95, :110-111), so the
+ * bf16 activation never goes to memory. `scale` is a device pointer to one float; out_dtype must
+ * be MAS_DTYPE_FP8_E4M3; out_stride is in bytes (= elements).
+ */
+MAS_API int mas_silu_and_mul_quant(void* out, const void* input, const float* scale, int64_t num_tokens,
+                           int64_t d, int64_t out_stride, int64_t input_stride, int dtype,
+                           int out_dtype, int enable_pdl, void* stream);
+
+/*
  * Rotary embedding applied in place to q and k from an fp32 cos|sin cache
  * ([max_positions, rotary_dim]: cos in columns [0, rotary_dim/2), sin in [rotary_dim/2, rotary_dim)).
  * Neox (is_neox=1): for i < rotary_dim/2, with c = cache[pos, i], s = cache[pos, rotary_dim/2 + i]:

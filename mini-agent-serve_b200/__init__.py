@@ -30,6 +30,7 @@ from .ops import (
     fused_add_rmsnorm_quant,
     read_status,
     silu_and_mul,
+    silu_and_mul_quant,
     status_word,
 )
 from .rope_cache import plain_cos_sin_cache, yarn_cos_sin_cache
@@ -52,6 +53,7 @@ __all__ = [
     "read_status",
     "rope_cache",
     "silu_and_mul",
+    "silu_and_mul_quant",
     "status_string",
     "status_word",
     "version",

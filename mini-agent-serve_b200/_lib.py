@@ -45,6 +45,7 @@ SIGNATURES: dict[str, tuple[type, list[type]]] = {
     "mas_fused_add_rmsnorm_quant": (
         _i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _i32, _vp]),
     "mas_silu_and_mul": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
+    "mas_silu_and_mul_quant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _vp]),
     "mas_rope_cos_sin_cache_inplace": (
         _i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                _i32, _i32, _vp, _i32, _vp]),

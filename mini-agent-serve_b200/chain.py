@@ -66,12 +66,12 @@ class ChainShape:
 
         norm: read x, r; write r and y (bf16: 8 B/elem; fp8 out: 7 B/elem) + the weight once;
         rope: read+write q and k, one fp32 cos|sin row and one int32 position per token;
-        silu: read gate and up, write out (6 B per output element).
+        silu: read gate and up, write out (6 B per output element; 5 B with the fp8 output).
         """
         H, I, D = self.hidden_size, self.intermediate_size, self.head_dim
         norm = (7 if quant else 8) * tokens * H + 2 * H
         rope = tokens * (2 * 2 * (self.q_size + self.kv_size) + 4 * D + 4)
-        silu = 6 * tokens * I
+        silu = (5 if quant else 6) * tokens * I
         return 2 * norm + rope + silu
 
     def embed_bytes(self, tokens: int, id_bytes: int = 8) -> int:
@@ -94,15 +94,18 @@ class ChainBuffers:
     cos_sin_cache: torch.Tensor  # (P, D) fp32
     w_in: torch.Tensor         # (L, H) input_layernorm weights
     w_post: torch.Tensor       # (L, H) post_attention_layernorm weights
-    x_fp8: Optional[torch.Tensor] = None    # (T, H) e4m3, quantised-norm form only
-    act_scale: Optional[torch.Tensor] = None  # (2,) fp32 activation scales (qkv_proj, gate_up_proj)
+    x_fp8: Optional[torch.Tensor] = None    # (T, H) e4m3, quantised form only
+    act_fp8: Optional[torch.Tensor] = None  # (T, I) e4m3 down_proj input, quantised form only
+    act_scale: Optional[torch.Tensor] = None  # (3,) fp32 activation scales (qkv, gate_up, down proj)
 
 
 class LayerChain:
     """One model step's per-token ops over `ChainBuffers` (see the module docstring).
 
     quant=False uses the bf16 fused_add_rmsnorm for both per-layer norms (in place on hidden and
-    attn_out); quant=True uses fused_add_rmsnorm_quant into x_fp8, as the decoder layers do.
+    attn_out) and the bf16 silu_and_mul; quant=True uses fused_add_rmsnorm_quant into x_fp8, as the
+    decoder layers do, and -- when act_fp8 is given -- silu_and_mul_quant into act_fp8, which is
+    down_proj's quantize_fp8 (devstral2.py:110-111) fused into the activation.
     """
 
     def __init__(self, shape: ChainShape, quant: bool = False, layers: Optional[int] = None):
@@ -127,7 +130,10 @@ class LayerChain:
             ops.fused_add_rmsnorm_quant(b.x_fp8, b.attn_out, b.residual, b.w_post[l], b.act_scale[1:2], eps)
         else:
             ops.fused_add_rmsnorm(b.attn_out, b.residual, b.w_post[l], eps)
-        ops.silu_and_mul(b.gate_up, out=b.act)
+        if self.quant and b.act_fp8 is not None:
+            ops.silu_and_mul_quant(b.gate_up, b.act_scale[2:3], out=b.act_fp8)
+        else:
+            ops.silu_and_mul(b.gate_up, out=b.act)
 
     def step(self, b: ChainBuffers) -> None:
         """embed -> residual = 0 -> layers x (norm, rope, norm, silu)."""

@@ -378,7 +378,8 @@ int mas_fused_add_rmsnorm_quant(void* out, const void* input, void* residual, co
   return run_norm<__half, true>(a, *st, fast_ok, stream, enable_pdl);
 }
 
-int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+// One launch of SiLU-and-mul; `scale` != nullptr selects the e4m3 output (quant) form.
+static int silu_impl(void* out, const void* input, const float* scale, int64_t num_tokens, int64_t d,
                      int64_t out_stride, int64_t input_stride, int dtype, int enable_pdl,
                      void* stream) {
   if (num_tokens < 0 || d < 0 || d > (INT32_MAX / 2)) return MAS_ERR_INVALID_ARGUMENT;
@@ -389,19 +390,26 @@ int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
   DeviceState* st = nullptr;
   int rc = current_device(&st);
   if (rc != MAS_OK) return rc;
+  const bool quant = scale != nullptr;
   SiluArgs a = {};
   a.out = out; a.in = input; a.rows = num_tokens; a.in_stride = input_stride;
-  a.out_stride = out_stride; a.d = (int32_t)d; a.fault = st->fault;
-  const bool vec = d % 8 == 0 && aligned(out, 16) && aligned(input, 16) && input_stride % 8 == 0 &&
+  a.out_stride = out_stride; a.d = (int32_t)d; a.fault = st->fault; a.scale = scale;
+  const int out_align = quant ? 8 : 16;
+  const bool vec = d % 8 == 0 && aligned(out, out_align) && aligned(input, 16) && input_stride % 8 == 0 &&
                    out_stride % 8 == 0;
   static const bool use_ring = env_is("MAS_SILU_IMPL", "ring");
-  if (vec && !use_ring) {
+  const bool bf16 = dtype == MAS_DTYPE_BF16;
+  if (vec && (quant || !use_ring)) {
     static const int env_rows = env_int("MAS_SILU_GRID_ROWS", 0);
-    const unsigned gx = (unsigned)ceil_div(d / 8, kSiluThreads);
-    const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, env_rows > 0 ? env_rows : 65535);
-    if (dtype == MAS_DTYPE_BF16)
-      return launch(silu_mul_vec_kernel<__nv_bfloat16>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
-    return launch(silu_mul_vec_kernel<__half>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+    const dim3 grid((unsigned)ceil_div(d / 8, kSiluThreads),
+                    (unsigned)std::min<int64_t>(num_tokens, env_rows > 0 ? env_rows : 65535));
+    const dim3 block(kSiluThreads);
+    if (quant) {
+      return bf16 ? launch(silu_mul_vec_kernel<__nv_bfloat16, true>, grid, block, 0, stream, enable_pdl, a)
+                  : launch(silu_mul_vec_kernel<__half, true>, grid, block, 0, stream, enable_pdl, a);
+    }
+    return bf16 ? launch(silu_mul_vec_kernel<__nv_bfloat16, false>, grid, block, 0, stream, enable_pdl, a)
+                : launch(silu_mul_vec_kernel<__half, false>, grid, block, 0, stream, enable_pdl, a);
   }
   if (vec) {
     static const int env_stages = env_int("MAS_SILU_STAGES", 0);
@@ -409,8 +417,8 @@ int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
     const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 6));
     const size_t smem = silu_ring_smem_bytes(stages, 2);
     int ctas = env_ctas > 0 ? env_ctas : (int)std::max<size_t>(1, kRingBytesPerSm / smem);
-    const void* fn = dtype == MAS_DTYPE_BF16 ? (const void*)silu_mul_ring_kernel<__nv_bfloat16>
-                                             : (const void*)silu_mul_ring_kernel<__half>;
+    const void* fn = bf16 ? (const void*)silu_mul_ring_kernel<__nv_bfloat16>
+                          : (const void*)silu_mul_ring_kernel<__half>;
     ctas = std::min(ctas, resident_ctas(fn, kSiluRingThreads, smem));
     const int64_t tiles = num_tokens * ceil_div(d, kSiluChunk);
     int64_t grid = std::min<int64_t>(tiles, (int64_t)st->sm_count * ctas);
@@ -418,16 +426,35 @@ int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
     grid = ceil_div(tiles, a.tiles_per_cta);
     a.stages = stages;
     if (smem <= kMaxSmemPerCta) {
-      if (dtype == MAS_DTYPE_BF16)
-        return launch(silu_mul_ring_kernel<__nv_bfloat16>, dim3((unsigned)grid), dim3(kSiluRingThreads), smem, stream, enable_pdl, a);
-      return launch(silu_mul_ring_kernel<__half>, dim3((unsigned)grid), dim3(kSiluRingThreads), smem, stream, enable_pdl, a);
+      return bf16 ? launch(silu_mul_ring_kernel<__nv_bfloat16>, dim3((unsigned)grid), dim3(kSiluRingThreads), smem,
+                           stream, enable_pdl, a)
+                  : launch(silu_mul_ring_kernel<__half>, dim3((unsigned)grid), dim3(kSiluRingThreads), smem, stream,
+                           enable_pdl, a);
     }
   }
-  const unsigned gy = (unsigned)std::min<int64_t>(num_tokens, 65535);
-  const unsigned gx = (unsigned)std::min<int64_t>(ceil_div(d, kSiluThreads), 1 << 16);
-  if (dtype == MAS_DTYPE_BF16)
-    return launch(silu_mul_generic_kernel<__nv_bfloat16>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
-  return launch(silu_mul_generic_kernel<__half>, dim3(gx, gy), dim3(kSiluThreads), 0, stream, enable_pdl, a);
+  const dim3 grid((unsigned)std::min<int64_t>(ceil_div(d, kSiluThreads), 1 << 16),
+                  (unsigned)std::min<int64_t>(num_tokens, 65535));
+  const dim3 block(kSiluThreads);
+  if (quant) {
+    return bf16 ? launch(silu_mul_generic_kernel<__nv_bfloat16, true>, grid, block, 0, stream, enable_pdl, a)
+                : launch(silu_mul_generic_kernel<__half, true>, grid, block, 0, stream, enable_pdl, a);
+  }
+  return bf16 ? launch(silu_mul_generic_kernel<__nv_bfloat16, false>, grid, block, 0, stream, enable_pdl, a)
+              : launch(silu_mul_generic_kernel<__half, false>, grid, block, 0, stream, enable_pdl, a);
+}
+
+int mas_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d,
+                     int64_t out_stride, int64_t input_stride, int dtype, int enable_pdl,
+                     void* stream) {
+  return silu_impl(out, input, nullptr, num_tokens, d, out_stride, input_stride, dtype, enable_pdl, stream);
+}
+
+int mas_silu_and_mul_quant(void* out, const void* input, const float* scale, int64_t num_tokens,
+                           int64_t d, int64_t out_stride, int64_t input_stride, int dtype,
+                           int out_dtype, int enable_pdl, void* stream) {
+  if (out_dtype != MAS_DTYPE_FP8_E4M3) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (!scale) return MAS_ERR_INVALID_ARGUMENT;
+  return silu_impl(out, input, scale, num_tokens, d, out_stride, input_stride, dtype, enable_pdl, stream);
 }
 
 // Rotation (and, when q_beta != 0, the llama-4 query scale) of every rotary pair: one launch.

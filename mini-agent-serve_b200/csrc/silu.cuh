@@ -31,6 +31,7 @@ struct SiluArgs {
   int32_t stages;          // TMA ring
   int64_t tiles_per_cta;   // TMA ring
   int32_t* fault;
+  const float* scale;      // quant variant: activation scale (device scalar)
 };
 
 // flashinfer compiles `val / (1.0f + __expf(-val))` with fast math, which makes the quotient the
@@ -124,14 +125,25 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
   pdl_launch_dependents();
 }
 
+// FP8Linear's activation quantisation of one silu output (rounded to the activation type first):
+// (act / scale) in fp32 with an IEEE quotient, clamped to +-448 and rounded to nearest even e4m3
+// (satfinite does the clamp; NaN stays NaN, as with a clamp that propagates it).
+__device__ __forceinline__ uint32_t quant4_e4m3(const float* act, float scale) {
+  return (uint32_t)f2_to_e4m3x2(__fdiv_rn(act[0], scale), __fdiv_rn(act[1], scale)) |
+         ((uint32_t)f2_to_e4m3x2(__fdiv_rn(act[2], scale), __fdiv_rn(act[3], scale)) << 16);
+}
+
 // Register variant (the default fast path): one 16-byte gate/up pair per thread and row, 32
 // registers, so 2048 threads per SM keep 64 KB of loads in flight; a 2-D grid of (256-vector column
-// blocks, row groups), each thread walking the rows of its group.
-template <typename T>
+// blocks, row groups), each thread walking the rows of its group. QUANT writes 8 e4m3 bytes per
+// thread instead of 8 activations.
+template <typename T, bool QUANT>
 __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const SiluArgs a) {
   pdl_wait();
   const int nvec = a.d >> 3;
   const int v = blockIdx.x * kSiluThreads + threadIdx.x;
+  float scale = 1.0f;
+  if constexpr (QUANT) scale = *a.scale;
   if (v < nvec) {
     for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
       const T* g = static_cast<const T*>(a.in) + row * a.in_stride + (size_t)v * 8;
@@ -142,21 +154,36 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
       unpack8<T>(uv, uf);
 #pragma unroll
       for (int e = 0; e < 8; ++e) y[e] = silu_f32(gf[e]) * uf[e];
-      st_plain(static_cast<T*>(a.out) + row * a.out_stride + (size_t)v * 8, pack8<T>(y));
+      if constexpr (QUANT) {
+        unpack8<T>(pack8<T>(y), y);  // the activation as the unfused op would have stored it
+        uint2 q;
+        q.x = quant4_e4m3(y, scale);
+        q.y = quant4_e4m3(y + 4, scale);
+        *reinterpret_cast<uint2*>(static_cast<uint8_t*>(a.out) + row * a.out_stride + (size_t)v * 8) = q;
+      } else {
+        st_plain(static_cast<T*>(a.out) + row * a.out_stride + (size_t)v * 8, pack8<T>(y));
+      }
     }
   }
   pdl_launch_dependents();
 }
 
-template <typename T>
+template <typename T, bool QUANT>
 __global__ void __launch_bounds__(kSiluThreads) silu_mul_generic_kernel(const SiluArgs a) {
   pdl_wait();
+  float scale = 1.0f;
+  if constexpr (QUANT) scale = *a.scale;
   for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
     const uint16_t* g = static_cast<const uint16_t*>(a.in) + row * a.in_stride;
     const uint16_t* u = g + a.d;
-    uint16_t* o = static_cast<uint16_t*>(a.out) + row * a.out_stride;
     for (int i = blockIdx.x * kSiluThreads + threadIdx.x; i < a.d; i += gridDim.x * kSiluThreads) {
-      o[i] = Elem<T>::from_f(silu_f32(Elem<T>::to_f(g[i])) * Elem<T>::to_f(u[i]));
+      const uint16_t act = Elem<T>::from_f(silu_f32(Elem<T>::to_f(g[i])) * Elem<T>::to_f(u[i]));
+      if constexpr (QUANT) {
+        static_cast<uint8_t*>(a.out)[row * a.out_stride + i] =
+            (uint8_t)(f2_to_e4m3x2(__fdiv_rn(Elem<T>::to_f(act), scale), 0.f) & 0xffu);
+      } else {
+        static_cast<uint16_t*>(a.out)[row * a.out_stride + i] = act;
+      }
     }
   }
   pdl_launch_dependents();

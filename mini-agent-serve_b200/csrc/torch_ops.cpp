@@ -94,6 +94,17 @@ void silu_and_mul(at::Tensor out, at::Tensor input, bool enable_pdl) {
         "mas_silu_and_mul");
 }
 
+void silu_and_mul_quant(at::Tensor out, at::Tensor input, at::Tensor scale, bool enable_pdl) {
+  const c10::cuda::CUDAGuard guard(input.device());
+  const Rows o = rows_of(out, "out"), x = rows_of(input, "input");
+  TORCH_CHECK(o.rows == x.rows && x.cols == 2 * o.cols, "mas_b200: out must be input[..., :d]-shaped");
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn, "mas_b200: out must be float8_e4m3fn");
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.numel() == 1, "mas_b200: scale must be one fp32 value");
+  check(mas_silu_and_mul_quant(out.data_ptr(), input.data_ptr(), scale.data_ptr<float>(), x.rows, o.cols, o.stride,
+                               x.stride, act_code(input), MAS_DTYPE_FP8_E4M3, enable_pdl, stream_of(input)),
+        "mas_silu_and_mul_quant");
+}
+
 void apply_rope_pos_ids_cos_sin_cache(at::Tensor q, at::Tensor k, at::Tensor cos_sin_cache, at::Tensor pos_ids,
                                       bool interleave, bool enable_pdl, std::optional<at::Tensor> status) {
   const c10::cuda::CUDAGuard guard(q.device());
@@ -177,6 +188,7 @@ TORCH_LIBRARY(mas_b200, m) {
   m.def("fused_add_rmsnorm_quant(Tensor(a!) out, Tensor input, Tensor(b!) residual, Tensor weight, Tensor scale, "
         "float eps, bool enable_pdl) -> ()");
   m.def("silu_and_mul(Tensor(a!) out, Tensor input, bool enable_pdl) -> ()");
+  m.def("silu_and_mul_quant(Tensor(a!) out, Tensor input, Tensor scale, bool enable_pdl) -> ()");
   m.def("apply_rope_pos_ids_cos_sin_cache(Tensor(a!) q, Tensor(b!) k, Tensor cos_sin_cache, Tensor pos_ids, "
         "bool interleave, bool enable_pdl, Tensor(c!)? status) -> ()");
   m.def("apply_rope_q_scale(Tensor(a!) q, Tensor(b!) k, Tensor cos_sin_cache, Tensor pos_ids, bool interleave, "
@@ -191,6 +203,7 @@ TORCH_LIBRARY_IMPL(mas_b200, CUDA, m) {
   m.impl("fused_add_rmsnorm", &fused_add_rmsnorm);
   m.impl("fused_add_rmsnorm_quant", &fused_add_rmsnorm_quant);
   m.impl("silu_and_mul", &silu_and_mul);
+  m.impl("silu_and_mul_quant", &silu_and_mul_quant);
   m.impl("apply_rope_pos_ids_cos_sin_cache", &apply_rope_pos_ids_cos_sin_cache);
   m.impl("apply_rope_q_scale", &apply_rope_q_scale);
   m.impl("embedding", &embedding);

@@ -33,6 +33,7 @@ __all__ = [
     "fused_add_rmsnorm",
     "fused_add_rmsnorm_quant",
     "silu_and_mul",
+    "silu_and_mul_quant",
     "apply_rope_with_cos_sin_cache_inplace",
     "apply_rope_and_llama4_query_scale_inplace",
     "embedding",
@@ -109,6 +110,7 @@ def _(input, residual, weight, eps, enable_pdl) -> None:
 _OP_NORM = torch.ops.mas_b200.fused_add_rmsnorm.default
 _OP_NORM_QUANT = torch.ops.mas_b200.fused_add_rmsnorm_quant.default
 _OP_SILU = torch.ops.mas_b200.silu_and_mul.default
+_OP_SILU_QUANT = torch.ops.mas_b200.silu_and_mul_quant.default
 _OP_ROPE = torch.ops.mas_b200.apply_rope_pos_ids_cos_sin_cache.default
 _OP_ROPE_QS = torch.ops.mas_b200.apply_rope_q_scale.default
 _OP_EMBED = torch.ops.mas_b200.embedding.default
@@ -211,6 +213,35 @@ def silu_and_mul(input: torch.Tensor, out: Optional[torch.Tensor] = None,
         out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), device=input.device, dtype=input.dtype)
     _act_code(input)
     _OP_SILU(out, input, True if enable_pdl is None else bool(enable_pdl))
+    return out
+
+
+@torch.library.register_fake("mas_b200::silu_and_mul_quant")
+def _(out, input, scale, enable_pdl) -> None:
+    return None
+
+
+def silu_and_mul_quant(input: torch.Tensor, scale: Union[float, torch.Tensor], out: Optional[torch.Tensor] = None,
+                       enable_pdl: Optional[bool] = None) -> torch.Tensor:
+    r"""SiLU-and-mul fused with the fp8 (e4m3) activation quantisation of the layer that consumes it.
+
+    Equal, bit for bit, to ``quantize_fp8(silu_and_mul(input), scale)`` -- the pair
+    Devstral2MLP.forward -> FP8Linear.forward runs (devstral2.py:224, :110-111, quantize_fp8 at
+    :93-95: ``(x / scale).clamp(-448, 448).to(float8_e4m3fn)``) -- in one pass, so the bf16/fp16
+    activation is never written. `scale` is FP8Linear's ``activation_scale`` (a 0-dim or (1,) fp32
+    tensor). Returns `out`, allocated as float8_e4m3fn when not given.
+    """
+    if input.shape[-1] * input.dtype.itemsize % 16 != 0:
+        raise ValueError("The pointers must be multiple of 16 bytes.")
+    if out is not None:
+        _check_shape(input, out)
+        if out.dtype != FP8:
+            raise ValueError(f"out must be {FP8}, got {out.dtype}")
+    else:
+        out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), device=input.device, dtype=FP8)
+    _act_code(input)
+    scale = _normalize_scale(scale, input)
+    _OP_SILU_QUANT(out, input, scale, True if enable_pdl is None else bool(enable_pdl))
     return out
 
 

@@ -133,5 +133,6 @@ def chain_buffers(ids: torch.Tensor, positions: torch.Tensor, device="cuda", see
     )
     if quant:
         b.x_fp8 = torch.empty((T, s.hidden_size), dtype=torch.float8_e4m3fn, device=device)
-        b.act_scale = torch.tensor([0.05, 0.05], dtype=torch.float32, device=device)
+        b.act_fp8 = torch.empty((T, s.intermediate_size), dtype=torch.float8_e4m3fn, device=device)
+        b.act_scale = torch.tensor([0.05, 0.05, 0.0137], dtype=torch.float32, device=device)
     return b

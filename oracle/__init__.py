@@ -58,6 +58,7 @@ _SIGS = {
     "orc_fused_add_rmsnorm": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32]),
     "orc_fused_add_rmsnorm_quant": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, _i32]),
     "orc_silu_and_mul": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i32]),
+    "orc_silu_and_mul_quant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32]),
     "orc_rope_cos_sin_cache_inplace": (
         _i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "orc_rope_cos_sin_cache_q_scale_inplace": (
@@ -138,6 +139,19 @@ def silu_and_mul(input: torch.Tensor, out: torch.Tensor | None = None) -> torch.
     x, o = _rows(input), _rows(out)
     _ok(lib().orc_silu_and_mul(o.data_ptr(), x.data_ptr(), x.shape[0], d, o.stride(0), x.stride(0), _ACT[x.dtype]),
         "silu_and_mul")
+    return out
+
+
+def silu_and_mul_quant(input: torch.Tensor, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu_and_mul then quantize_fp8 with `scale`: e4m3 bytes as a torch.float8_e4m3fn tensor."""
+    _cpu(input, "input")
+    d = input.shape[-1] // 2
+    if out is None:
+        out = torch.empty(input.shape[:-1] + (d,), dtype=torch.float8_e4m3fn)
+    x, o = _rows(input), _rows(out)
+    s = torch.tensor([float(scale)], dtype=torch.float32)
+    _ok(lib().orc_silu_and_mul_quant(o.data_ptr(), x.data_ptr(), s.data_ptr(), x.shape[0], d, o.stride(0),
+                                     x.stride(0), _ACT[x.dtype]), "silu_and_mul_quant")
     return out
 
 

@@ -192,6 +192,38 @@ int orc_silu_and_mul(void* out, const void* input, int64_t num_tokens, int64_t d
 }
 
 /* ---------------------------------------------------------------------------------------------
+ * SiLU-and-mul followed by FP8Linear's activation quantisation, one pass: the reference computes
+ *   act = silu_and_mul(gate_up)                 (devstral2.py:224, rounded to bf16/fp16 as above)
+ *   x   = quantize_fp8(act, activation_scale)  (devstral2.py:93-95 via FP8Linear.forward :110-111)
+ *       = (act / scale).clamp(-448, 448).to(float8_e4m3fn)
+ * where torch.compile computes the quotient in fp32 from the upcast activation (IEEE divide, no
+ * intermediate rounding to the activation type), clamps (NaN passes through) and converts with
+ * round-to-nearest-even. The e4m3 bytes go to out[t * out_stride + i].
+ * --------------------------------------------------------------------------------------------- */
+int orc_silu_and_mul_quant(void* out, const void* input, const float* scale, int64_t num_tokens,
+                           int64_t d, int64_t out_stride, int64_t input_stride, int dtype) {
+  if (num_tokens < 0 || d < 0 || (dtype != ORC_BF16 && dtype != ORC_FP16) || !scale) return -1;
+  const float sc = *scale;
+#pragma omp parallel for schedule(static)
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    const uint16_t* g = (const uint16_t*)input + t * input_stride;
+    const uint16_t* u = g + d;
+    uint8_t* o = (uint8_t*)out + t * out_stride;
+    for (int64_t i = 0; i < d; ++i) {
+      const float gv = ld_act(&g[i], dtype);
+      const float e = (float)exp(-(double)gv);
+      const float den = 1.0f + e;
+      const float s = den >= 0x1p126f ? gv * 0.0f : gv / den;
+      const float act = ld_act_from(to_act(s * ld_act(&u[i], dtype), dtype), dtype);
+      float q = act / sc;
+      if (q == q) q = q < -448.0f ? -448.0f : (q > 448.0f ? 448.0f : q);
+      o[i] = orc_f32_to_e4m3(q);
+    }
+  }
+  return 0;
+}
+
+/* ---------------------------------------------------------------------------------------------
  * Rotary embedding from the fp32 cos|sin cache. FI/data/include/flashinfer/pos_enc.cuh:129-147
  * (neox: element i pairs with i + rotary_dim/2), :218-234 (interleaved: 2i pairs with 2i+1), cache
  * row layout :375-391 (cos = cache[pos, i], sin = cache[pos, rotary_dim/2 + i]):

@@ -47,6 +47,23 @@ def test_norm_matches_flashinfer(name):
     assert_ulp(xo, _t(Z[f"norm_{name}_xout"], dtype), what=f"{name} output")
 
 
+@pytest.mark.parametrize("name", _cases("siluq"))
+def test_silu_quant_matches_reference_pair(name):
+    """silu_and_mul -> the reference's compiled quantize_fp8 (devstral2.py:93-95) on a B200: the
+    oracle's activation within 1 ulp and its e4m3 bytes within one step (bit-exact where the
+    activations agree)."""
+    xin = _t(Z[f"siluq_{name}_in"], torch.bfloat16)
+    scale = float(Z[f"siluq_{name}_scale"])
+    act = _t(Z[f"siluq_{name}_act"], torch.bfloat16)
+    want = _t(Z[f"siluq_{name}_out"], torch.float8_e4m3fn)
+    got = oracle.silu_and_mul_quant(xin, scale)
+    assert_ulp(oracle.silu_and_mul(xin), act, what=f"siluq {name} activation")
+    assert_ulp(got, want, what=f"siluq {name} e4m3")
+    # from the reference's own activation the oracle's quantisation is exact
+    same = (oracle.silu_and_mul(xin).view(torch.int16) == act.view(torch.int16))
+    assert torch.equal(got.view(torch.uint8)[same], want.view(torch.uint8)[same])
+
+
 @pytest.mark.parametrize("name", _cases("quant"))
 def test_norm_quant_matches_flashinfer(name):
     x, r, w = (_t(Z[f"quant_{name}_{k}"], torch.bfloat16) for k in ("x", "r", "w"))

@@ -166,10 +166,11 @@ def test_chain_torch_compile_matches_eager(cuda):
 
 
 def test_chain_quant_form_graph(cuda):
-    """The fp8-out norms the decoder layers call, captured in a graph (scale read on the device)."""
+    """The fp8-out norms and the fp8-out SiLU-mul, captured in a graph (scales read on the device)."""
     b = _small_buffers(cuda)
     b.x_fp8 = torch.empty(b.hidden.shape, dtype=torch.float8_e4m3fn, device=cuda)
-    b.act_scale = torch.tensor([0.05, 0.1], device=cuda)
+    b.act_fp8 = torch.empty(b.act.shape, dtype=torch.float8_e4m3fn, device=cuda)
+    b.act_scale = torch.tensor([0.05, 0.1, 0.02], device=cuda)
     chain = LayerChain(SMALL, quant=True, layers=1)
     mas_b200.embedding_out(b.hidden, b.ids, b.table)
     ref_in = (b.hidden.cpu(), b.residual.cpu())
@@ -186,3 +187,4 @@ def test_chain_quant_form_graph(cuda):
     oracle.fused_add_rmsnorm_quant(out, attn_before, r, b.w_post[0].cpu(), 0.1, SMALL.rms_norm_eps)
     assert_bits_equal(b.residual.cpu(), r, "residual")
     assert_ulp(b.x_fp8.cpu(), out, what="fp8 out of the post-attention norm")
+    assert_ulp(b.act_fp8.cpu(), oracle.silu_and_mul_quant(b.gate_up.cpu(), 0.02), what="fp8 SiLU-mul")

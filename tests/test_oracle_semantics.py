@@ -102,6 +102,27 @@ def test_silu(shape, scale):
                what="silu")
 
 
+@pytest.mark.parametrize("scale", [1e-3, 0.0137, 0.5, 400.0])
+def test_silu_quant_is_quantize_fp8_of_silu(scale):
+    """silu_and_mul_quant == quantize_fp8(silu_and_mul(x), scale) (devstral2.py:93-95) bit for bit,
+    with the quotient in fp32 from the upcast activation; saturation and subnormal ranges included."""
+    x = (torch.randn(9, 2 * 48, generator=torch.Generator().manual_seed(6)) * 4).to(torch.bfloat16)
+    act = oracle.silu_and_mul(x)
+    want = (act.float() / torch.tensor(scale, dtype=torch.float32)).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    assert_bits_equal(oracle.silu_and_mul_quant(x, scale), want, f"scale {scale}")
+
+
+def test_silu_quant_nan_and_strides():
+    x = torch.randn(3, 2 * 16, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16)
+    x[1, 3] = float("nan")
+    q = oracle.silu_and_mul_quant(x, 0.1)
+    assert torch.isnan(q[1, 3].float()) and not torch.isnan(q[0].float()).any()
+    out = torch.zeros(3, 24, dtype=torch.float8_e4m3fn)
+    oracle.silu_and_mul_quant(x, 0.1, out=out[:, :16])
+    assert_bits_equal(out[:, :16], q, "strided out")
+    assert torch.count_nonzero(out[:, 16:].view(torch.uint8)) == 0
+
+
 @pytest.mark.parametrize("D,rd,neox,pdt", [(128, 128, True, torch.int32), (128, 128, False, torch.int64),
                                            (64, 32, True, torch.int32), (40, 40, False, torch.int32)])
 def test_rope(D, rd, neox, pdt):
