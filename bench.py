@@ -202,6 +202,19 @@ class FlashinferOps:
     def embedding_out(out, ids, table):
         return torch.index_select(table, 0, ids, out=out.view(-1, table.shape[1]))
 
+    @staticmethod
+    def apply_rope_and_append_paged_kv_cache(positions, q, k, v, head_size, cache, batch_indices, paged_kv_cache,
+                                             kv_indices, kv_indptr, kv_last_page_len, **_):
+        """The reference's unfused pair: flashinfer rope, then flashinfer append_paged_kv_cache
+        (devstral2.py:163-173)."""
+        from flashinfer.page import append_paged_kv_cache
+        from flashinfer.rope import apply_rope_with_cos_sin_cache_inplace
+
+        T = q.shape[0]
+        apply_rope_with_cos_sin_cache_inplace(positions, q, k, head_size, cache, is_neox=True)
+        append_paged_kv_cache(k.view(T, -1, head_size), v.view(T, -1, head_size), batch_indices, positions,
+                              paged_kv_cache, kv_indices, kv_indptr, kv_last_page_len, kv_layout="NHD")
+
     _quantize = None
 
     def silu_and_mul_quant(self, x, scale, out=None, enable_pdl=True):
@@ -375,6 +388,19 @@ class OpWorkload:
             self.bytes = self.T * (2 * 2 * (self.q.shape[1] + self.k.shape[1]) + 4 * 128 + 4)
             self.cfg = {"workload": "config 3 rope q[T,32,128] k[T,8,128]", "tokens": self.T,
                         "l2": "inputs larger than L2 (689 MB)"}
+        elif name == "rope_append":
+            self.pb, self.qkv, self.cache, self.kc, self.vc = wl.rope_append_inputs(device)
+            Hq, Hkv, D = 32, 8, 128
+            self.q = self.qkv[:, : Hq * D]
+            self.k = self.qkv[:, Hq * D: (Hq + Hkv) * D]
+            self.v = self.qkv[:, (Hq + Hkv) * D:]
+            self.kv_indices = self.pb.kv_indices.contiguous()
+            self.T = self.qkv.shape[0]
+            # q read+write, k read + write back + cache write, v read + cache write, cos|sin row,
+            # position, batch index, page-table entry
+            self.bytes = self.T * (2 * 2 * Hq * D + 3 * 2 * Hkv * D + 2 * 2 * Hkv * D + 4 * D + 12)
+            self.cfg = {"workload": "config 3 rope q[T,32,128] k[T,8,128] + paged KV append (NHD, 16-token pages)",
+                        "tokens": self.T, "pages": self.pb.num_pages, "l2": "inputs larger than L2"}
         elif name == "embed":
             self.table, self.ids = wl.embed_inputs(device)
             self.T = self.ids.shape[0]
@@ -411,6 +437,11 @@ class OpWorkload:
             o.silu_and_mul_quant(self.x, self.scale, out=self.out, enable_pdl=True)
         elif n == "rope":
             o.apply_rope_with_cos_sin_cache_inplace(self.pos, self.q, self.k, 128, self.cache, is_neox=True)
+        elif n == "rope_append":
+            pb = self.pb
+            o.apply_rope_and_append_paged_kv_cache(pb.positions, self.q, self.k, self.v, 128, self.cache,
+                                                   pb.batch_indices, (self.kc, self.vc), self.kv_indices,
+                                                   pb.kv_indptr, pb.kv_last_page_len)
         elif n == "embed":
             o.embedding_out(self.out, self.ids, self.table)
         if dom_events is not None:
@@ -652,7 +683,8 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["mas", "reference", "flashinfer"], default="mas")
     ap.add_argument("--workload", choices=["chain", "norm", "norm_fp8", "silu", "rope", "embed", "norm_chain",
-                                           "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain"], default="chain")
+                                           "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain", "rope_append"],
+                    default="chain")
     ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -52,6 +52,7 @@ extern "C" {
 #define MAS_STATUS_EMBED_ID_OUT_OF_RANGE 1 /* an id outside [0, vocab): its output row is zeroed */
 #define MAS_STATUS_ROPE_POS_OUT_OF_RANGE 2 /* a position outside [0, max_positions): token left as is */
 #define MAS_STATUS_COPY_TIMEOUT 4          /* a bulk-copy wait ran past its time limit; outputs undefined */
+#define MAS_STATUS_KV_SLOT_OUT_OF_RANGE 8  /* a paged-KV slot index out of range: that token not appended */
 
 /* Library version, (major << 16) | minor. */
 MAS_API int mas_version(void);
@@ -189,6 +190,70 @@ MAS_API int mas_embedding_gather_fill_placeholders(void* out, const void* table,
                                                    int64_t num_tokens, int64_t hidden_size, int64_t vocab_size,
                                                    int64_t out_stride, int64_t table_stride, int elem_size,
                                                    int32_t* status, int enable_pdl, void* stream);
+
+/*
+ * The paged KV cache of one attention layer, as flashinfer's paged_kv_t describes it
+ * (FI/data/include/flashinfer/page.cuh:161-165): k and v element [page, entry, head, feature] at
+ * page * stride_page + entry * stride_entry + head * stride_head + feature (elements; the NHD layout
+ * [num_pages, page_size, heads, head_size] has stride_entry = heads * head_size, stride_head =
+ * head_size; HND swaps them). kv_indices (int32, num_indices entries) lists the pages of every
+ * sequence back to back, sequence b's starting at kv_indptr[b] (int32, batch_size + 1 entries).
+ * Devstral2Model.forward passes block_tables.flatten() and arange(batch + 1) * max_blocks
+ * (miniagentserve/models/devstral2/devstral2.py:172, :289).
+ */
+typedef struct MasPagedKVCache {
+  void* k_cache;
+  void* v_cache;
+  int64_t num_pages;
+  int64_t page_size;
+  int64_t stride_page;
+  int64_t stride_entry;
+  int64_t stride_head;
+  const int32_t* kv_indices;
+  int64_t num_indices;
+  const int32_t* kv_indptr;
+  int64_t batch_size;
+} MasPagedKVCache;
+
+/*
+ * Appends token t's k and v rows to the paged cache: with b = batch_indices[t] (int32) and
+ * p = positions[t] (int32 or int64, positions_dtype), flat = kv_indptr[b] * page_size + p,
+ * page = kv_indices[flat / page_size], entry = flat % page_size, then k_cache[page, entry, h, :] =
+ * key[t, h, :] and the same for v (byte-exact copies). k/v element (t, h, f) at
+ * t * stride_token + h * stride_head + f. A token whose batch index, position, page slot or page id
+ * is out of range is not appended and sets MAS_STATUS_KV_SLOT_OUT_OF_RANGE in *status (if not NULL).
+ * Replaces flashinfer.page.append_paged_kv_cache (FI/page.py:280-406; kernel
+ * FI/data/include/flashinfer/page.cuh:259-284), called once per attention layer
+ * (miniagentserve/models/devstral2/devstral2.py:170-173). dtype: BF16 or FP16 for k, v and the cache.
+ */
+MAS_API int mas_append_paged_kv_cache(const void* key, const void* value, const int32_t* batch_indices,
+                                      const void* positions, int positions_dtype, const MasPagedKVCache* cache,
+                                      int64_t num_tokens, int64_t num_kv_heads, int64_t head_size,
+                                      int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_token,
+                                      int64_t v_stride_head, int dtype, int32_t* status, int enable_pdl,
+                                      void* stream);
+
+/*
+ * Rope (and, when q_scale_beta != 0, the llama-4 query scale) on q and k in place, fused with the
+ * paged KV append of the rotated k and of v: one launch where the layout allows it (q, k and v heads
+ * contiguous within a token, 16-byte aligned rows and cache strides), otherwise the rope launch
+ * followed by the append launch. Equal to mas_rope_cos_sin_cache_q_scale_inplace (or
+ * mas_rope_cos_sin_cache_inplace when q_scale_beta == 0) followed by mas_append_paged_kv_cache,
+ * except that a token whose position is outside [0, max_positions) is neither rotated nor appended
+ * (MAS_STATUS_ROPE_POS_OUT_OF_RANGE). Replaces the sequence apply_rope_with_cos_sin_cache_inplace
+ * -> append_paged_kv_cache -> llama-4 query scaling of Devstral2Attention.forward
+ * (miniagentserve/models/devstral2/devstral2.py:163-179); q_scale_original_max must be > 0 when
+ * q_scale_beta != 0.
+ */
+MAS_API int mas_rope_append_paged_kv_cache(const void* positions, int positions_dtype, void* query, void* key,
+                                           const void* value, const float* cos_sin_cache,
+                                           const int32_t* batch_indices, const MasPagedKVCache* cache,
+                                           int64_t num_tokens, int64_t num_q_heads, int64_t num_kv_heads,
+                                           int64_t head_size, int64_t rotary_dim, int64_t max_positions,
+                                           int64_t q_stride_token, int64_t q_stride_head, int64_t k_stride_token,
+                                           int64_t k_stride_head, int64_t v_stride_token, int64_t v_stride_head,
+                                           int is_neox, float q_scale_beta, int64_t q_scale_original_max,
+                                           int dtype, int32_t* status, int enable_pdl, void* stream);
 
 #ifdef __cplusplus
 }

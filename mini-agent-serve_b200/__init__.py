@@ -23,6 +23,8 @@ from .embedding import Embedding
 from .ops import (
     apply_rope_and_llama4_query_scale_inplace,
     apply_rope_with_cos_sin_cache_inplace,
+    append_paged_kv_cache,
+    apply_rope_and_append_paged_kv_cache,
     embedding as embedding_gather,
     embedding_fill_placeholders,
     embedding_out,
@@ -40,6 +42,8 @@ __all__ = [
     "MasError",
     "apply_rope_and_llama4_query_scale_inplace",
     "apply_rope_with_cos_sin_cache_inplace",
+    "append_paged_kv_cache",
+    "apply_rope_and_append_paged_kv_cache",
     "chain",
     "embedding_fill_placeholders",
     "embedding_gather",

@@ -32,8 +32,20 @@ ERR_NO_DEVICE = -4
 STATUS_EMBED_ID_OUT_OF_RANGE = 1
 STATUS_ROPE_POS_OUT_OF_RANGE = 2
 STATUS_COPY_TIMEOUT = 4
+STATUS_KV_SLOT_OUT_OF_RANGE = 8
 
 _i32, _i64, _f32, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+
+
+class PagedKVCache(ctypes.Structure):
+    """struct MasPagedKVCache (include/mas_b200.h): one layer's paged k/v cache and page table."""
+
+    _fields_ = [("k_cache", _vp), ("v_cache", _vp), ("num_pages", _i64), ("page_size", _i64),
+                ("stride_page", _i64), ("stride_entry", _i64), ("stride_head", _i64), ("kv_indices", _vp),
+                ("num_indices", _i64), ("kv_indptr", _vp), ("batch_size", _i64)]
+
+
+_kvp = ctypes.POINTER(PagedKVCache)
 
 # Every exported function with its argument types, in header order.
 SIGNATURES: dict[str, tuple[type, list[type]]] = {
@@ -56,6 +68,11 @@ SIGNATURES: dict[str, tuple[type, list[type]]] = {
         _i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _i32, _vp]),
     "mas_embedding_gather_fill_placeholders": (
         _i32, [_vp, _vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _i32, _vp]),
+    "mas_append_paged_kv_cache": (
+        _i32, [_vp, _vp, _vp, _vp, _i32, _kvp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp, _i32, _vp]),
+    "mas_rope_append_paged_kv_cache": (
+        _i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _kvp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+               _i64, _i64, _i64, _i32, _f32, _i64, _i32, _vp, _i32, _vp]),
 }
 
 

@@ -77,6 +77,19 @@ cudaError_t opt_in_norm_row() {
   return e;
 }
 
+template <typename T>
+cudaError_t opt_in_rope_ring() {
+  cudaError_t e;
+  if ((e = opt_in_smem(rope_ring_kernel<T, int32_t, true, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<T, int32_t, false, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<T, int64_t, true, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<T, int64_t, false, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<T, int32_t, true, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<T, int32_t, false, true>)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(rope_ring_kernel<T, int64_t, true, true>)) != cudaSuccess) return e;
+  return opt_in_smem(rope_ring_kernel<T, int64_t, false, true>);
+}
+
 cudaError_t prepare_current(DeviceState& st, int device) {
   cudaError_t e = cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, device);
   if (e != cudaSuccess) return e;
@@ -90,14 +103,8 @@ cudaError_t prepare_current(DeviceState& st, int device) {
   if ((e = opt_in_norm_row<__half, true>()) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__nv_bfloat16>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(silu_mul_ring_kernel<__half>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int32_t, true>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int32_t, false>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int64_t, true>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(rope_ring_kernel<__nv_bfloat16, int64_t, false>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(rope_ring_kernel<__half, int32_t, true>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(rope_ring_kernel<__half, int32_t, false>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(rope_ring_kernel<__half, int64_t, true>)) != cudaSuccess) return e;
-  if ((e = opt_in_smem(rope_ring_kernel<__half, int64_t, false>)) != cudaSuccess) return e;
+  if ((e = opt_in_rope_ring<__nv_bfloat16>()) != cudaSuccess) return e;
+  if ((e = opt_in_rope_ring<__half>()) != cudaSuccess) return e;
   if ((e = opt_in_smem(embed_tma_kernel<int32_t>)) != cudaSuccess) return e;
   if ((e = opt_in_smem(embed_tma_kernel<int64_t>)) != cudaSuccess) return e;
   void* fault = nullptr;
@@ -292,6 +299,108 @@ int check_act_dtype(int dtype) {
   return (dtype == MAS_DTYPE_BF16 || dtype == MAS_DTYPE_FP16) ? MAS_OK : MAS_ERR_UNSUPPORTED_DTYPE;
 }
 
+// Launches the token-staged rope ring (APPEND: fused with the paged KV append) when its shared
+// memory fits; returns kNotLaunched otherwise.
+constexpr int kNotLaunched = -1000;  // neither a MAS_ERR_* code nor a cudaError_t
+
+template <bool APPEND>
+int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState* st, void* stream,
+                       int enable_pdl) {
+  const uint32_t stage = rope_stage_bytes(r.Hq, r.Hkv, r.D, r.rd, 2, APPEND);
+  static const int env_stages = env_int("MAS_ROPE_STAGES", 0);
+  const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
+  const size_t per_cta = rope_ring_smem_bytes(stage, stages, kRopeMaxTokensPerCta, APPEND);
+  if (per_cta > kMaxSmemPerCta) return kNotLaunched;
+  const void* fn = bf ? (i64 ? (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, true, APPEND>
+                                     : (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, false, APPEND>)
+                             : (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int32_t, true, APPEND>
+                                     : (const void*)rope_ring_kernel<__nv_bfloat16, int32_t, false, APPEND>))
+                      : (i64 ? (neox ? (const void*)rope_ring_kernel<__half, int64_t, true, APPEND>
+                                     : (const void*)rope_ring_kernel<__half, int64_t, false, APPEND>)
+                             : (neox ? (const void*)rope_ring_kernel<__half, int32_t, true, APPEND>
+                                     : (const void*)rope_ring_kernel<__half, int32_t, false, APPEND>));
+  int ctas = (int)std::max<size_t>(1, kRingBytesPerSm / per_cta);
+  ctas = std::min(ctas, resident_ctas(fn, kRopeRingThreads, per_cta));
+  int64_t grid = std::max<int64_t>((int64_t)st->sm_count * ctas, ceil_div(r.T, kRopeMaxTokensPerCta));
+  grid = std::min<int64_t>(grid, r.T);
+  r.tokens_per_cta = (int32_t)ceil_div(r.T, grid);
+  grid = ceil_div(r.T, r.tokens_per_cta);
+  r.stages = stages;
+  const size_t smem = rope_ring_smem_bytes(stage, stages, r.tokens_per_cta, APPEND);
+  const dim3 g((unsigned)grid), b(kRopeRingThreads);
+  if (bf) {
+    if (i64) return neox ? launch(rope_ring_kernel<__nv_bfloat16, int64_t, true, APPEND>, g, b, smem, stream, enable_pdl, r)
+                         : launch(rope_ring_kernel<__nv_bfloat16, int64_t, false, APPEND>, g, b, smem, stream, enable_pdl, r);
+    return neox ? launch(rope_ring_kernel<__nv_bfloat16, int32_t, true, APPEND>, g, b, smem, stream, enable_pdl, r)
+                : launch(rope_ring_kernel<__nv_bfloat16, int32_t, false, APPEND>, g, b, smem, stream, enable_pdl, r);
+  }
+  if (i64) return neox ? launch(rope_ring_kernel<__half, int64_t, true, APPEND>, g, b, smem, stream, enable_pdl, r)
+                       : launch(rope_ring_kernel<__half, int64_t, false, APPEND>, g, b, smem, stream, enable_pdl, r);
+  return neox ? launch(rope_ring_kernel<__half, int32_t, true, APPEND>, g, b, smem, stream, enable_pdl, r)
+              : launch(rope_ring_kernel<__half, int32_t, false, APPEND>, g, b, smem, stream, enable_pdl, r);
+}
+
+int launch_rope_ring(const RopeRingArgs& r, bool append, bool bf, bool i64, bool neox, DeviceState* st,
+                     void* stream, int enable_pdl) {
+  return append ? launch_rope_ring_t<true>(r, bf, i64, neox, st, stream, enable_pdl)
+                : launch_rope_ring_t<false>(r, bf, i64, neox, st, stream, enable_pdl);
+}
+
+// Whether the fused ring can also append: v heads contiguous within a token, 16-byte aligned v rows
+// and cache rows.
+bool append_ring_ok(const AppendArgs& a, int64_t head_size) {
+  return (a.Hkv == 0 || (a.vsh == head_size && aligned(a.v, 16) && a.vsn % 8 == 0)) &&
+         aligned(a.kv.k_cache, 16) && aligned(a.kv.v_cache, 16) && a.kv.stride_page % 8 == 0 &&
+         a.kv.stride_entry % 8 == 0 && a.kv.stride_head % 8 == 0;
+}
+
+int launch_append(const AppendArgs& a, bool bf, bool i64, DeviceState* st, void* stream, int enable_pdl) {
+  if (a.T == 0 || a.Hkv == 0) return MAS_OK;
+  const bool vec = a.D % 8 == 0 && aligned(a.k, 16) && aligned(a.v, 16) && a.ksn % 8 == 0 && a.ksh % 8 == 0 &&
+                   a.vsn % 8 == 0 && a.vsh % 8 == 0 && aligned(a.kv.k_cache, 16) && aligned(a.kv.v_cache, 16) &&
+                   a.kv.stride_page % 8 == 0 && a.kv.stride_entry % 8 == 0 && a.kv.stride_head % 8 == 0;
+  const dim3 blk(kAppendThreads);
+  if (vec) {
+    // a warp per token, grid-strided over at most 8 CTAs of 8 warps per SM
+    const int64_t warps_per_cta = kAppendThreads / 32;
+    const dim3 grid((unsigned)std::min<int64_t>(ceil_div(a.T, warps_per_cta), (int64_t)st->sm_count * 8));
+    if (bf) return i64 ? launch(append_kv_vec_kernel<__nv_bfloat16, int64_t>, grid, blk, 0, stream, enable_pdl, a)
+                       : launch(append_kv_vec_kernel<__nv_bfloat16, int32_t>, grid, blk, 0, stream, enable_pdl, a);
+    return i64 ? launch(append_kv_vec_kernel<__half, int64_t>, grid, blk, 0, stream, enable_pdl, a)
+               : launch(append_kv_vec_kernel<__half, int32_t>, grid, blk, 0, stream, enable_pdl, a);
+  }
+  const dim3 grid((unsigned)std::min<int64_t>(ceil_div(a.T * a.Hkv * a.D, kAppendThreads), 1 << 22));
+  if (bf) return i64 ? launch(append_kv_generic_kernel<__nv_bfloat16, int64_t>, grid, blk, 0, stream, enable_pdl, a)
+                     : launch(append_kv_generic_kernel<__nv_bfloat16, int32_t>, grid, blk, 0, stream, enable_pdl, a);
+  return i64 ? launch(append_kv_generic_kernel<__half, int64_t>, grid, blk, 0, stream, enable_pdl, a)
+             : launch(append_kv_generic_kernel<__half, int32_t>, grid, blk, 0, stream, enable_pdl, a);
+}
+
+// Checks a MasPagedKVCache and the k/v layout, and fills AppendArgs (all but k, v and positions).
+int make_append_args(AppendArgs* out, const MasPagedKVCache* c, const int32_t* batch_indices,
+                     int64_t num_tokens, int64_t num_kv_heads, int64_t head_size, int64_t k_stride_token,
+                     int64_t k_stride_head, int64_t v_stride_token, int64_t v_stride_head, int32_t* status) {
+  if (!c || num_tokens < 0 || num_kv_heads < 0 || head_size <= 0 || num_kv_heads > INT32_MAX ||
+      head_size > INT32_MAX)
+    return MAS_ERR_INVALID_ARGUMENT;
+  if (num_tokens > 0 && num_kv_heads > 0) {
+    if (!c->k_cache || !c->v_cache || !c->kv_indices || !c->kv_indptr || !batch_indices)
+      return MAS_ERR_INVALID_ARGUMENT;
+    if (c->page_size <= 0 || c->num_pages < 0 || c->num_indices < 0 || c->batch_size < 0 ||
+        c->stride_page < 0 || c->stride_entry < 0 || c->stride_head < 0)
+      return MAS_ERR_INVALID_ARGUMENT;
+  }
+  AppendArgs a = {};
+  a.T = num_tokens; a.ksn = k_stride_token; a.ksh = k_stride_head; a.vsn = v_stride_token; a.vsh = v_stride_head;
+  a.Hkv = (int32_t)num_kv_heads; a.D = (int32_t)head_size; a.status = status;
+  a.kv.k_cache = c->k_cache; a.kv.v_cache = c->v_cache; a.kv.num_pages = c->num_pages;
+  a.kv.page_size = c->page_size; a.kv.stride_page = c->stride_page; a.kv.stride_entry = c->stride_entry;
+  a.kv.stride_head = c->stride_head; a.kv.kv_indices = c->kv_indices; a.kv.num_indices = c->num_indices;
+  a.kv.kv_indptr = c->kv_indptr; a.kv.batch_size = c->batch_size; a.kv.batch_indices = batch_indices;
+  *out = a;
+  return MAS_OK;
+}
+
 }  // namespace
 }  // namespace mas
 
@@ -463,7 +572,8 @@ static int rope_main(const void* positions, int positions_dtype, void* query, vo
                      int64_t num_kv_heads, int64_t head_size, int64_t rotary_dim,
                      int64_t max_positions, int64_t q_stride_token, int64_t q_stride_head,
                      int64_t k_stride_token, int64_t k_stride_head, int is_neox, int dtype,
-                     int32_t* status, int enable_pdl, void* stream, float q_beta, float q_inv_orig) {
+                     int32_t* status, int enable_pdl, void* stream, float q_beta, float q_inv_orig,
+                     const AppendArgs* app = nullptr) {
   if (num_tokens < 0 || num_q_heads < 0 || num_kv_heads < 0 || head_size <= 0 ||
       max_positions < 0 || num_q_heads + num_kv_heads > INT32_MAX)
     return MAS_ERR_INVALID_ARGUMENT;
@@ -510,45 +620,28 @@ static int rope_main(const void* positions, int positions_dtype, void* query, vo
   const bool ring = vec && !force_vec && head_size % 8 == 0 &&
                     (num_q_heads == 0 || q_stride_head == head_size) &&
                     (num_kv_heads == 0 || k_stride_head == head_size);
-  if (ring) {
+  if (ring && (!app || append_ring_ok(*app, head_size))) {
     RopeRingArgs r = {};
     r.pos = positions; r.q = query; r.k = key; r.cache = cos_sin_cache; r.T = num_tokens; r.P = max_positions;
     r.qsn = q_stride_token; r.ksn = k_stride_token; r.Hq = (int32_t)num_q_heads; r.Hkv = (int32_t)num_kv_heads;
     r.D = (int32_t)head_size; r.rd = (int32_t)rotary_dim; r.status = status; r.fault = st->fault;
     r.q_beta = q_beta; r.q_inv_orig = q_inv_orig;
-    const uint32_t stage = rope_stage_bytes(r.Hq, r.Hkv, r.D, r.rd, 2);
-    static const int env_stages = env_int("MAS_ROPE_STAGES", 0);
-    const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
-    const size_t per_cta = rope_ring_smem_bytes(stage, stages, kRopeMaxTokensPerCta);
-    if (per_cta <= kMaxSmemPerCta) {
-      const void* fn = bf ? (i64 ? (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, true>
-                                         : (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, false>)
-                                 : (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int32_t, true>
-                                         : (const void*)rope_ring_kernel<__nv_bfloat16, int32_t, false>))
-                          : (i64 ? (neox ? (const void*)rope_ring_kernel<__half, int64_t, true>
-                                         : (const void*)rope_ring_kernel<__half, int64_t, false>)
-                                 : (neox ? (const void*)rope_ring_kernel<__half, int32_t, true>
-                                         : (const void*)rope_ring_kernel<__half, int32_t, false>));
-      int ctas = (int)std::max<size_t>(1, kRingBytesPerSm / per_cta);
-      ctas = std::min(ctas, resident_ctas(fn, kRopeRingThreads, per_cta));
-      int64_t grid = std::max<int64_t>((int64_t)st->sm_count * ctas, ceil_div(num_tokens, kRopeMaxTokensPerCta));
-      grid = std::min<int64_t>(grid, num_tokens);
-      r.tokens_per_cta = (int32_t)ceil_div(num_tokens, grid);
-      grid = ceil_div(num_tokens, r.tokens_per_cta);
-      r.stages = stages;
-      const size_t smem = rope_ring_smem_bytes(stage, stages, r.tokens_per_cta);
-      const dim3 g((unsigned)grid), b(kRopeRingThreads);
-      if (bf) {
-        if (i64) return neox ? launch(rope_ring_kernel<__nv_bfloat16, int64_t, true>, g, b, smem, stream, enable_pdl, r)
-                             : launch(rope_ring_kernel<__nv_bfloat16, int64_t, false>, g, b, smem, stream, enable_pdl, r);
-        return neox ? launch(rope_ring_kernel<__nv_bfloat16, int32_t, true>, g, b, smem, stream, enable_pdl, r)
-                    : launch(rope_ring_kernel<__nv_bfloat16, int32_t, false>, g, b, smem, stream, enable_pdl, r);
-      }
-      if (i64) return neox ? launch(rope_ring_kernel<__half, int64_t, true>, g, b, smem, stream, enable_pdl, r)
-                           : launch(rope_ring_kernel<__half, int64_t, false>, g, b, smem, stream, enable_pdl, r);
-      return neox ? launch(rope_ring_kernel<__half, int32_t, true>, g, b, smem, stream, enable_pdl, r)
-                  : launch(rope_ring_kernel<__half, int32_t, false>, g, b, smem, stream, enable_pdl, r);
+    if (app) {
+      r.v = app->v; r.vsn = app->vsn; r.kv = app->kv;
     }
+    const int rc_ring = launch_rope_ring(r, app != nullptr, bf, i64, neox, st, stream, enable_pdl);
+    if (rc_ring != kNotLaunched) return rc_ring;
+  }
+  if (app) {
+    // Unfused: the rope launch, then the append launch (tokens that rope skipped stay unappended).
+    const int rc2 = rope_main(positions, positions_dtype, query, key, cos_sin_cache, num_tokens, num_q_heads,
+                              num_kv_heads, head_size, rotary_dim, max_positions, q_stride_token, q_stride_head,
+                              k_stride_token, k_stride_head, is_neox, dtype, status, enable_pdl, stream, q_beta,
+                              q_inv_orig, nullptr);
+    if (rc2 != MAS_OK || max_positions == 0) return rc2;
+    AppendArgs ap = *app;
+    ap.pos_limit = max_positions;
+    return launch_append(ap, bf, i64, st, stream, enable_pdl);
   }
   if (vec) {
     a.tpu = (int32_t)(rotary_dim / 16);
@@ -574,21 +667,24 @@ int mas_rope_cos_sin_cache_inplace(const void* positions, int positions_dtype, v
                    k_stride_token, k_stride_head, is_neox, dtype, status, enable_pdl, stream, 0.f, 0.f);
 }
 
-int mas_rope_cos_sin_cache_q_scale_inplace(const void* positions, int positions_dtype, void* query,
-                                           void* key, const float* cos_sin_cache, int64_t num_tokens,
-                                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
-                                           int64_t rotary_dim, int64_t max_positions,
-                                           int64_t q_stride_token, int64_t q_stride_head,
-                                           int64_t k_stride_token, int64_t k_stride_head, int is_neox,
-                                           float q_scale_beta, int64_t q_scale_original_max, int dtype,
-                                           int32_t* status, int enable_pdl, void* stream) {
-  if (q_scale_original_max <= 0) return MAS_ERR_INVALID_ARGUMENT;
-  // torch divides a CUDA tensor by a host scalar as a multiplication by the fp32 reciprocal.
-  const float inv_orig = 1.0f / (float)q_scale_original_max;
+// Rope with the llama-4 query scale (optionally fused with the paged append), plus the element-wise
+// scale of the q elements past rotary_dim when the rotary part is partial.
+static int rope_q_scale_impl(const void* positions, int positions_dtype, void* query, void* key,
+                             const float* cos_sin_cache, int64_t num_tokens, int64_t num_q_heads,
+                             int64_t num_kv_heads, int64_t head_size, int64_t rotary_dim, int64_t max_positions,
+                             int64_t q_stride_token, int64_t q_stride_head, int64_t k_stride_token,
+                             int64_t k_stride_head, int is_neox, float q_scale_beta, int64_t q_scale_original_max,
+                             int dtype, int32_t* status, int enable_pdl, void* stream, const AppendArgs* app) {
+  float inv_orig = 0.f;
+  if (q_scale_beta != 0.f) {
+    if (q_scale_original_max <= 0) return MAS_ERR_INVALID_ARGUMENT;
+    // torch divides a CUDA tensor by a host scalar as a multiplication by the fp32 reciprocal.
+    inv_orig = 1.0f / (float)q_scale_original_max;
+  }
   int rc = rope_main(positions, positions_dtype, query, key, cos_sin_cache, num_tokens, num_q_heads,
                      num_kv_heads, head_size, rotary_dim, max_positions, q_stride_token, q_stride_head,
                      k_stride_token, k_stride_head, is_neox, dtype, status, enable_pdl, stream,
-                     q_scale_beta, inv_orig);
+                     q_scale_beta, inv_orig, app);
   if (rc != MAS_OK || q_scale_beta == 0.f || rotary_dim >= head_size || num_q_heads == 0 || num_tokens == 0)
     return rc;
   // Partial rotary: the elements past rotary_dim are scaled by a second, element-wise launch.
@@ -604,6 +700,62 @@ int mas_rope_cos_sin_cache_q_scale_inplace(const void* positions, int positions_
                      : launch(rope_q_tail_scale_kernel<__nv_bfloat16, int32_t>, grid, dim3(kRopeThreads), 0, stream, enable_pdl, a, hs);
   return i64 ? launch(rope_q_tail_scale_kernel<__half, int64_t>, grid, dim3(kRopeThreads), 0, stream, enable_pdl, a, hs)
              : launch(rope_q_tail_scale_kernel<__half, int32_t>, grid, dim3(kRopeThreads), 0, stream, enable_pdl, a, hs);
+}
+
+int mas_rope_cos_sin_cache_q_scale_inplace(const void* positions, int positions_dtype, void* query,
+                                           void* key, const float* cos_sin_cache, int64_t num_tokens,
+                                           int64_t num_q_heads, int64_t num_kv_heads, int64_t head_size,
+                                           int64_t rotary_dim, int64_t max_positions,
+                                           int64_t q_stride_token, int64_t q_stride_head,
+                                           int64_t k_stride_token, int64_t k_stride_head, int is_neox,
+                                           float q_scale_beta, int64_t q_scale_original_max, int dtype,
+                                           int32_t* status, int enable_pdl, void* stream) {
+  if (q_scale_original_max <= 0) return MAS_ERR_INVALID_ARGUMENT;
+  return rope_q_scale_impl(positions, positions_dtype, query, key, cos_sin_cache, num_tokens, num_q_heads,
+                           num_kv_heads, head_size, rotary_dim, max_positions, q_stride_token, q_stride_head,
+                           k_stride_token, k_stride_head, is_neox, q_scale_beta, q_scale_original_max, dtype,
+                           status, enable_pdl, stream, nullptr);
+}
+
+int mas_append_paged_kv_cache(const void* key, const void* value, const int32_t* batch_indices,
+                              const void* positions, int positions_dtype, const MasPagedKVCache* cache,
+                              int64_t num_tokens, int64_t num_kv_heads, int64_t head_size,
+                              int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_token,
+                              int64_t v_stride_head, int dtype, int32_t* status, int enable_pdl,
+                              void* stream) {
+  if (check_act_dtype(dtype) != MAS_OK) return MAS_ERR_UNSUPPORTED_DTYPE;
+  if (positions_dtype != MAS_DTYPE_INT32 && positions_dtype != MAS_DTYPE_INT64) return MAS_ERR_UNSUPPORTED_DTYPE;
+  AppendArgs a;
+  int rc = make_append_args(&a, cache, batch_indices, num_tokens, num_kv_heads, head_size, k_stride_token,
+                            k_stride_head, v_stride_token, v_stride_head, status);
+  if (rc != MAS_OK) return rc;
+  if (num_tokens == 0 || num_kv_heads == 0) return MAS_OK;
+  if (!key || !value || !positions) return MAS_ERR_INVALID_ARGUMENT;
+  a.k = key; a.v = value; a.pos = positions;
+  DeviceState* st = nullptr;
+  if ((rc = current_device(&st)) != MAS_OK) return rc;
+  return launch_append(a, dtype == MAS_DTYPE_BF16, positions_dtype == MAS_DTYPE_INT64, st, stream, enable_pdl);
+}
+
+int mas_rope_append_paged_kv_cache(const void* positions, int positions_dtype, void* query, void* key,
+                                   const void* value, const float* cos_sin_cache, const int32_t* batch_indices,
+                                   const MasPagedKVCache* cache, int64_t num_tokens, int64_t num_q_heads,
+                                   int64_t num_kv_heads, int64_t head_size, int64_t rotary_dim,
+                                   int64_t max_positions, int64_t q_stride_token, int64_t q_stride_head,
+                                   int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_token,
+                                   int64_t v_stride_head, int is_neox, float q_scale_beta,
+                                   int64_t q_scale_original_max, int dtype, int32_t* status, int enable_pdl,
+                                   void* stream) {
+  AppendArgs a;
+  int rc = make_append_args(&a, cache, batch_indices, num_tokens, num_kv_heads, head_size, k_stride_token,
+                            k_stride_head, v_stride_token, v_stride_head, status);
+  if (rc != MAS_OK) return rc;
+  if (num_tokens > 0 && num_kv_heads > 0 && !value) return MAS_ERR_INVALID_ARGUMENT;
+  a.k = key; a.v = value; a.pos = positions;
+  return rope_q_scale_impl(positions, positions_dtype, query, key, cos_sin_cache, num_tokens, num_q_heads,
+                           num_kv_heads, head_size, rotary_dim, max_positions, q_stride_token, q_stride_head,
+                           k_stride_token, k_stride_head, is_neox, q_scale_beta, q_scale_original_max, dtype,
+                           status, enable_pdl, stream, num_kv_heads > 0 ? &a : nullptr);
 }
 
 static int gather_impl(void* out, const void* table, const void* ids, int ids_dtype,

@@ -16,6 +16,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "paged_kv.cuh"
 
 namespace mas {
 
@@ -162,6 +163,11 @@ __global__ void __launch_bounds__(kRopeThreads) rope_vec_kernel(const RopeArgs a
 // the token from shared memory (cos/sin included), store the results to q/k with 16-byte stores,
 // and release the stage on its `empty` mbarrier. A token whose position is out of range gets no
 // copies and no stores. Every wait is bounded.
+//
+// APPEND fuses the paged KV append that follows rope in the attention layer (paged_kv.cuh): the
+// token's v row is staged too and its cache slot is computed in the position pre-pass, the rotated
+// k vectors go to the k cache as well as back to k, and the consumers copy the k tail past
+// rotary_dim and the v heads from shared memory into the cache. k and v are read from HBM once.
 struct RopeRingArgs {
   const void* pos;
   void* q;
@@ -177,31 +183,37 @@ struct RopeRingArgs {
   int32_t* fault;
   float q_beta;      // llama-4 query scale (0: off), see llama4_q_scale
   float q_inv_orig;
+  const void* v;     // APPEND: v rows (heads contiguous), token stride vsn
+  int64_t vsn;
+  PagedKVArgs kv;
 };
 
 constexpr int kRopeConsumerWarps = 8;
 constexpr int kRopeRingThreads = 32 * (1 + kRopeConsumerWarps);
 constexpr int kRopeMaxTokensPerCta = 2048;
 
-__host__ __device__ inline uint32_t rope_stage_bytes(int Hq, int Hkv, int D, int rd, int elem_bytes) {
-  return (uint32_t)((Hq + Hkv) * D * elem_bytes + rd * 4);
+__host__ __device__ inline uint32_t rope_stage_bytes(int Hq, int Hkv, int D, int rd, int elem_bytes, bool append) {
+  return (uint32_t)((Hq + Hkv + (append ? Hkv : 0)) * D * elem_bytes + rd * 4);
 }
-__host__ __device__ inline size_t rope_ring_smem_bytes(uint32_t stage, int stages, int tokens_per_cta) {
-  return (size_t)stages * stage + (size_t)stages * 16 + (size_t)tokens_per_cta * 8;
+// Per token: its position (and, with APPEND, its cache slot) as int64.
+__host__ __device__ inline size_t rope_ring_smem_bytes(uint32_t stage, int stages, int tokens_per_cta, bool append) {
+  return (size_t)stages * stage + (size_t)stages * 16 + (size_t)tokens_per_cta * (append ? 16 : 8);
 }
 
-template <typename T, typename PosT, bool NEOX>
+template <typename T, typename PosT, bool NEOX, bool APPEND>
 __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeRingArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int S = a.stages;
   const int NH = a.Hq + a.Hkv;
   const uint32_t q_bytes = (uint32_t)(a.Hq * a.D) * (uint32_t)sizeof(T);
   const uint32_t k_bytes = (uint32_t)(a.Hkv * a.D) * (uint32_t)sizeof(T);
+  const uint32_t v_bytes = APPEND ? k_bytes : 0u;
   const uint32_t c_bytes = (uint32_t)a.rd * 4u;
-  const uint32_t stage_bytes = q_bytes + k_bytes + c_bytes;
+  const uint32_t stage_bytes = q_bytes + k_bytes + v_bytes + c_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
   uint64_t* empty = full + S;
   int64_t* spos = reinterpret_cast<int64_t*>(empty + S);
+  int64_t* sslot = spos + a.tokens_per_cta;  // APPEND only
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const int64_t tok0 = (int64_t)blockIdx.x * a.tokens_per_cta;
@@ -221,6 +233,14 @@ __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeR
     const bool valid = pos >= 0 && pos < a.P;
     if (!valid) flag_status(a.status, MAS_STATUS_ROPE_POS_OUT_OF_RANGE);
     spos[i] = valid ? pos : -1;
+    if constexpr (APPEND) {
+      int64_t slot = -1;
+      if (valid) {
+        slot = kv_slot(a.kv, tok0 + i, pos);
+        if (slot < 0) flag_status(a.status, MAS_STATUS_KV_SLOT_OUT_OF_RANGE);
+      }
+      sslot[i] = slot;
+    }
   }
   __syncthreads();
 
@@ -241,10 +261,12 @@ __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeR
         }
         unsigned char* st = smem + (size_t)s * stage_bytes;
         const int64_t t = tok0 + i;
-        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        const bool with_v = APPEND && v_bytes != 0u && sslot[i] >= 0;
+        mbar_arrive_expect_tx(&full[s], stage_bytes - (with_v ? 0u : v_bytes));
         if (q_bytes) bulk_load(st, qb + t * a.qsn, q_bytes, &full[s]);
         if (k_bytes) bulk_load(st + q_bytes, kb + t * a.ksn, k_bytes, &full[s]);
-        bulk_load(st + q_bytes + k_bytes, a.cache + pos * a.rd, c_bytes, &full[s]);
+        if (with_v) bulk_load(st + q_bytes + k_bytes, static_cast<const T*>(a.v) + t * a.vsn, v_bytes, &full[s]);
+        bulk_load(st + q_bytes + k_bytes + v_bytes, a.cache + pos * a.rd, c_bytes, &full[s]);
       }
     }
   } else {
@@ -261,8 +283,9 @@ __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeR
       }
       if (spos[i] >= 0) {
         const unsigned char* st = smem + (size_t)s * stage_bytes;
-        const float* c = reinterpret_cast<const float*>(st + q_bytes + k_bytes);
+        const float* c = reinterpret_cast<const float*>(st + q_bytes + k_bytes + v_bytes);
         const int64_t t = tok0 + i;
+        const int64_t slot = APPEND ? sslot[i] : -1;
         const float qs = a.q_beta != 0.f ? llama4_q_scale<T>(spos[i], a.q_beta, a.q_inv_orig) : 0.f;
         for (int gi = ct; gi < groups; gi += ncons) {
           const int h = gi / tpu;
@@ -301,8 +324,38 @@ __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeR
               o1[e] = scaled_q<T>(o1[e], qs);
             }
           }
-          st_plain(gh + off0, pack8<T>(o0));
-          st_plain(gh + off1, pack8<T>(o1));
+          const Vec16 p0 = pack8<T>(o0), p1 = pack8<T>(o1);
+          st_plain(gh + off0, p0);
+          st_plain(gh + off1, p1);
+          if (APPEND && h >= a.Hq && slot >= 0) {
+            T* ch = static_cast<T*>(a.kv.k_cache) + slot + (int64_t)(h - a.Hq) * a.kv.stride_head;
+            st_plain(ch + off0, p0);
+            st_plain(ch + off1, p1);
+          }
+        }
+        if constexpr (APPEND) {
+          // the k tail past rotary_dim (unrotated) and every v head: staged rows -> cache
+          if (slot >= 0) {
+            const int tail_v = (a.D - a.rd) >> 3;  // 16-byte vectors per k head tail
+            const int d_v = a.D >> 3;               // 16-byte vectors per v head
+            const int n_tail = a.Hkv * tail_v;
+            const int n_copy = n_tail + a.Hkv * d_v;
+            const T* sk = reinterpret_cast<const T*>(st + q_bytes);
+            const T* sv = reinterpret_cast<const T*>(st + q_bytes + k_bytes);
+            for (int u = ct; u < n_copy; u += ncons) {
+              if (u < n_tail) {
+                const int h = u / tail_v, j = u - h * tail_v;
+                const int off = a.rd + j * 8;
+                st_plain(static_cast<T*>(a.kv.k_cache) + slot + (int64_t)h * a.kv.stride_head + off,
+                         *reinterpret_cast<const Vec16*>(sk + (size_t)h * a.D + off));
+              } else {
+                const int r = u - n_tail;
+                const int h = r / d_v, j = r - h * d_v;
+                st_plain(static_cast<T*>(a.kv.v_cache) + slot + (int64_t)h * a.kv.stride_head + j * 8,
+                         *reinterpret_cast<const Vec16*>(sv + (size_t)h * a.D + j * 8));
+              }
+            }
+          }
         }
       }
       __syncwarp();

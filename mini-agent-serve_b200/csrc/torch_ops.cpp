@@ -135,6 +135,82 @@ void apply_rope_q_scale(at::Tensor q, at::Tensor k, at::Tensor cos_sin_cache, at
         "mas_rope_cos_sin_cache_q_scale_inplace");
 }
 
+// One layer's paged cache as the C ABI describes it: 4-D k/v caches with identical strides, NHD
+// ([pages, page_size, heads, head_size]) or HND ([pages, heads, page_size, head_size]).
+MasPagedKVCache paged_cache(const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& kv_indices,
+                            const at::Tensor& kv_indptr, bool hnd) {
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4, "mas_b200: k_cache and v_cache must be 4-D");
+  TORCH_CHECK(k_cache.sizes() == v_cache.sizes() && k_cache.strides() == v_cache.strides(),
+              "mas_b200: k/v cache shapes and strides must be identical");
+  TORCH_CHECK(k_cache.stride(3) == 1, "mas_b200: the cache's last dimension must be contiguous");
+  TORCH_CHECK(kv_indices.scalar_type() == at::kInt && kv_indptr.scalar_type() == at::kInt &&
+                  kv_indices.is_contiguous() && kv_indptr.is_contiguous() && kv_indptr.dim() == 1 &&
+                  kv_indptr.numel() >= 1,
+              "mas_b200: kv_indices and kv_indptr must be contiguous int32 vectors");
+  MasPagedKVCache c = {};
+  c.k_cache = k_cache.data_ptr();
+  c.v_cache = v_cache.data_ptr();
+  c.num_pages = k_cache.size(0);
+  c.page_size = hnd ? k_cache.size(2) : k_cache.size(1);
+  c.stride_page = k_cache.stride(0);
+  c.stride_entry = hnd ? k_cache.stride(2) : k_cache.stride(1);
+  c.stride_head = hnd ? k_cache.stride(1) : k_cache.stride(2);
+  c.kv_indices = kv_indices.data_ptr<int32_t>();
+  c.num_indices = kv_indices.numel();
+  c.kv_indptr = kv_indptr.data_ptr<int32_t>();
+  c.batch_size = kv_indptr.numel() - 1;
+  return c;
+}
+
+void append_paged_kv_cache(at::Tensor k, at::Tensor v, at::Tensor batch_indices, at::Tensor positions,
+                           at::Tensor k_cache, at::Tensor v_cache, at::Tensor kv_indices, at::Tensor kv_indptr,
+                           bool hnd, bool enable_pdl, std::optional<at::Tensor> status) {
+  const c10::cuda::CUDAGuard guard(k.device());
+  TORCH_CHECK(k.dim() == 3 && v.dim() == 3 && k.sizes() == v.sizes(), "mas_b200: k and v must be (tokens, heads, head_size)");
+  TORCH_CHECK(k.stride(2) == 1 && v.stride(2) == 1, "mas_b200: k and v must be contiguous in head_size");
+  TORCH_CHECK(batch_indices.scalar_type() == at::kInt && batch_indices.is_contiguous() &&
+                  batch_indices.numel() == k.size(0) && positions.is_contiguous() && positions.numel() == k.size(0),
+              "mas_b200: batch_indices (int32) and positions must be contiguous, one per token");
+  TORCH_CHECK(k_cache.scalar_type() == k.scalar_type() && v.scalar_type() == k.scalar_type(),
+              "mas_b200: k, v and the caches must share one dtype");
+  const MasPagedKVCache c = paged_cache(k_cache, v_cache, kv_indices, kv_indptr, hnd);
+  TORCH_CHECK((hnd ? k_cache.size(1) : k_cache.size(2)) == k.size(1) && k_cache.size(3) == k.size(2),
+              "mas_b200: the cache's heads/head_size differ from k's");
+  int32_t* st = status.has_value() ? status->data_ptr<int32_t>() : nullptr;
+  check(mas_append_paged_kv_cache(k.data_ptr(), v.data_ptr(), batch_indices.data_ptr<int32_t>(), positions.data_ptr(),
+                                  id_code(positions), &c, k.size(0), k.size(1), k.size(2), k.stride(0), k.stride(1),
+                                  v.stride(0), v.stride(1), act_code(k), st, enable_pdl, stream_of(k)),
+        "mas_append_paged_kv_cache");
+}
+
+void rope_append_paged_kv_cache(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cos_sin_cache,
+                                at::Tensor pos_ids, at::Tensor batch_indices, at::Tensor k_cache, at::Tensor v_cache,
+                                at::Tensor kv_indices, at::Tensor kv_indptr, bool interleave, bool hnd, double beta,
+                                int64_t original_max, bool enable_pdl, std::optional<at::Tensor> status) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.dim() == 3, "mas_b200: q, k and v must be (tokens, heads, head_size) views");
+  TORCH_CHECK(k.sizes() == v.sizes() && q.size(2) == k.size(2) && q.size(0) == k.size(0),
+              "mas_b200: q, k and v shapes disagree");
+  TORCH_CHECK(cos_sin_cache.dim() == 2 && cos_sin_cache.is_contiguous(), "mas_b200: cos_sin_cache must be contiguous");
+  TORCH_CHECK(batch_indices.scalar_type() == at::kInt && batch_indices.is_contiguous() &&
+                  batch_indices.numel() == q.size(0) && pos_ids.is_contiguous() && pos_ids.numel() == q.size(0),
+              "mas_b200: batch_indices (int32) and positions must be contiguous, one per token");
+  TORCH_CHECK(k_cache.scalar_type() == k.scalar_type() && v.scalar_type() == k.scalar_type() &&
+                  q.scalar_type() == k.scalar_type(),
+              "mas_b200: q, k, v and the caches must share one dtype");
+  const MasPagedKVCache c = paged_cache(k_cache, v_cache, kv_indices, kv_indptr, hnd);
+  TORCH_CHECK((hnd ? k_cache.size(1) : k_cache.size(2)) == k.size(1) && k_cache.size(3) == k.size(2),
+              "mas_b200: the cache's heads/head_size differ from k's");
+  int32_t* st = status.has_value() ? status->data_ptr<int32_t>() : nullptr;
+  check(mas_rope_append_paged_kv_cache(
+            pos_ids.data_ptr(), id_code(pos_ids), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            cos_sin_cache.data_ptr<float>(), batch_indices.data_ptr<int32_t>(), &c, q.size(0), q.size(1), k.size(1),
+            q.size(2), cos_sin_cache.size(1), cos_sin_cache.size(0), q.stride(0), q.stride(1), k.stride(0), k.stride(1),
+            v.stride(0), v.stride(1), interleave ? 0 : 1, static_cast<float>(beta), original_max, act_code(q), st,
+            enable_pdl, stream_of(q)),
+        "mas_rope_append_paged_kv_cache");
+}
+
 void gather(at::Tensor& out, const at::Tensor& ids, const at::Tensor& weight, bool enable_pdl,
             const std::optional<at::Tensor>& status) {
   TORCH_CHECK(weight.dim() == 2 && weight.stride(1) == 1, "mas_b200: weight must be (num_embeddings, dim)");
@@ -193,6 +269,11 @@ TORCH_LIBRARY(mas_b200, m) {
         "bool interleave, bool enable_pdl, Tensor(c!)? status) -> ()");
   m.def("apply_rope_q_scale(Tensor(a!) q, Tensor(b!) k, Tensor cos_sin_cache, Tensor pos_ids, bool interleave, "
         "float beta, int original_max, bool enable_pdl, Tensor(c!)? status) -> ()");
+  m.def("append_paged_kv_cache(Tensor k, Tensor v, Tensor batch_indices, Tensor positions, Tensor(a!) k_cache, "
+        "Tensor(b!) v_cache, Tensor kv_indices, Tensor kv_indptr, bool hnd, bool enable_pdl, Tensor(c!)? status) -> ()");
+  m.def("rope_append_paged_kv_cache(Tensor(a!) q, Tensor(b!) k, Tensor v, Tensor cos_sin_cache, Tensor pos_ids, "
+        "Tensor batch_indices, Tensor(c!) k_cache, Tensor(d!) v_cache, Tensor kv_indices, Tensor kv_indptr, "
+        "bool interleave, bool hnd, float beta, int original_max, bool enable_pdl, Tensor(e!)? status) -> ()");
   m.def("embedding(Tensor input_ids, Tensor weight, bool enable_pdl, Tensor(a!)? status) -> Tensor");
   m.def("embedding_out(Tensor(a!) out, Tensor input_ids, Tensor weight, bool enable_pdl, Tensor(b!)? status) -> ()");
   m.def("embedding_fill(Tensor(a!) input_ids, Tensor weight, Tensor last_tokens, bool enable_pdl, "
@@ -206,6 +287,8 @@ TORCH_LIBRARY_IMPL(mas_b200, CUDA, m) {
   m.impl("silu_and_mul_quant", &silu_and_mul_quant);
   m.impl("apply_rope_pos_ids_cos_sin_cache", &apply_rope_pos_ids_cos_sin_cache);
   m.impl("apply_rope_q_scale", &apply_rope_q_scale);
+  m.impl("append_paged_kv_cache", &append_paged_kv_cache);
+  m.impl("rope_append_paged_kv_cache", &rope_append_paged_kv_cache);
   m.impl("embedding", &embedding);
   m.impl("embedding_out", &embedding_out);
   m.impl("embedding_fill", &embedding_fill);

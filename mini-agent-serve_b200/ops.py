@@ -36,6 +36,8 @@ __all__ = [
     "silu_and_mul_quant",
     "apply_rope_with_cos_sin_cache_inplace",
     "apply_rope_and_llama4_query_scale_inplace",
+    "append_paged_kv_cache",
+    "apply_rope_and_append_paged_kv_cache",
     "embedding",
     "embedding_out",
     "embedding_fill_placeholders",
@@ -113,6 +115,8 @@ _OP_SILU = torch.ops.mas_b200.silu_and_mul.default
 _OP_SILU_QUANT = torch.ops.mas_b200.silu_and_mul_quant.default
 _OP_ROPE = torch.ops.mas_b200.apply_rope_pos_ids_cos_sin_cache.default
 _OP_ROPE_QS = torch.ops.mas_b200.apply_rope_q_scale.default
+_OP_APPEND = torch.ops.mas_b200.append_paged_kv_cache.default
+_OP_ROPE_APPEND = torch.ops.mas_b200.rope_append_paged_kv_cache.default
 _OP_EMBED = torch.ops.mas_b200.embedding.default
 _OP_EMBED_OUT = torch.ops.mas_b200.embedding_out.default
 _OP_EMBED_FILL = torch.ops.mas_b200.embedding_fill.default
@@ -327,6 +331,140 @@ def apply_rope_and_llama4_query_scale_inplace(positions: torch.Tensor, query: to
     k = key.view(key.shape[0], -1, head_size)
     _OP_ROPE_QS(q, k, cos_sin_cache, positions, not is_neox, float(beta), int(original_max_position_embeddings),
                 True if enable_pdl is None else bool(enable_pdl), _status_arg(query.device))
+
+
+# ------------------------------------------------------------------------------------------------
+# Paged KV cache append (alone, and fused with rope).
+# ------------------------------------------------------------------------------------------------
+@torch.library.register_fake("mas_b200::append_paged_kv_cache")
+def _(k, v, batch_indices, positions, k_cache, v_cache, kv_indices, kv_indptr, hnd, enable_pdl, status) -> None:
+    return None
+
+
+@torch.library.register_fake("mas_b200::rope_append_paged_kv_cache")
+def _(q, k, v, cos_sin_cache, pos_ids, batch_indices, k_cache, v_cache, kv_indices, kv_indptr, interleave, hnd,
+      beta, original_max, enable_pdl, status) -> None:
+    return None
+
+
+def _unpack_paged_kv_cache(paged_kv_cache, kv_layout: str) -> tuple[torch.Tensor, torch.Tensor]:
+    """(k_cache, v_cache) from a tuple of 4-D tensors or one 5-D tensor with k/v on dimension 1
+    (FI/page.py:_unpack_paged_kv_cache)."""
+    if kv_layout not in ("NHD", "HND"):
+        raise KeyError(f"Invalid kv_layout {kv_layout}")
+    if isinstance(paged_kv_cache, tuple):
+        k_cache, v_cache = paged_kv_cache
+    elif torch.is_tensor(paged_kv_cache) and paged_kv_cache.dim() == 5:
+        k_cache, v_cache = paged_kv_cache[:, 0], paged_kv_cache[:, 1]
+    else:
+        raise KeyError("Unrecognized paged_kv_cache type or shape")
+    return k_cache, v_cache
+
+
+def _int32(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.int32 and t.is_contiguous() else t.int().contiguous()
+
+
+def _check_paged(k_cache: torch.Tensor, v_cache: torch.Tensor, kv_indptr: torch.Tensor,
+                 kv_last_page_len: torch.Tensor, heads: int, head_size: int, kv_layout: str, dtype) -> None:
+    if k_cache.dim() != 4 or k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride():
+        raise ValueError("k/v caches must be 4-D with identical shapes and strides")
+    if k_cache.dtype != dtype or v_cache.dtype != dtype:
+        raise ValueError(f"k/v caches must be {dtype}")
+    cache_heads = k_cache.shape[1] if kv_layout == "HND" else k_cache.shape[2]
+    if cache_heads != heads or k_cache.shape[3] != head_size:
+        raise ValueError(f"cache heads/head_dim {(cache_heads, k_cache.shape[3])} differ from {(heads, head_size)}")
+    if kv_indptr.dim() != 1 or kv_last_page_len.dim() != 1 or kv_indptr.shape[0] != kv_last_page_len.shape[0] + 1:
+        raise ValueError("kv_indptr must have batch_size + 1 entries, kv_last_page_len batch_size")
+
+
+def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor, batch_indices: torch.Tensor,
+                          positions: torch.Tensor, paged_kv_cache, kv_indices: torch.Tensor, kv_indptr: torch.Tensor,
+                          kv_last_page_len: torch.Tensor, kv_layout: str = "NHD",
+                          enable_pdl: Optional[bool] = None) -> None:
+    r"""Appends each token's k and v rows to the paged KV cache.
+
+    Same signature and meaning as flashinfer.page.append_paged_kv_cache (FI/page.py:280-406), as
+    Devstral2Attention.forward calls it (devstral2.py:170-173): token ``i`` of sequence
+    ``b = batch_indices[i]`` at ``positions[i]`` is written to entry ``p % page_size`` of page
+    ``kv_indices[kv_indptr[b] + p // page_size]`` of `paged_kv_cache` (a ``(k_cache, v_cache)`` tuple or
+    one 5-D tensor; layout NHD or HND). `append_key`/`append_value` are ``(nnz, num_kv_heads, head_dim)``
+    (strided views of a qkv row are fine). An out-of-range index skips that token and sets
+    STATUS_KV_SLOT_OUT_OF_RANGE in the device status word instead of writing out of bounds.
+    `enable_pdl` (an addition) defaults to True.
+    """
+    k_cache, v_cache = _unpack_paged_kv_cache(paged_kv_cache, kv_layout)
+    if append_key.dim() != 3 or append_value.shape != append_key.shape:
+        raise ValueError("append_key and append_value must be (nnz, num_kv_heads, head_dim) and equal in shape")
+    if append_key.dtype != append_value.dtype:
+        raise ValueError("append_key and append_value must share one dtype")
+    _act_code(append_key)
+    nnz, heads, head_size = append_key.shape
+    if batch_indices.shape != (nnz,) or positions.shape != (nnz,):
+        raise ValueError("batch_indices and positions must have one entry per appended token")
+    if positions.dtype not in _ID_DTYPES:
+        positions = positions.int()
+    _check_paged(k_cache, v_cache, kv_indptr, kv_last_page_len, heads, head_size, kv_layout, append_key.dtype)
+    if nnz == 0:
+        return
+    _OP_APPEND(append_key, append_value, _int32(batch_indices), positions.contiguous(), k_cache, v_cache,
+               _int32(kv_indices), _int32(kv_indptr), kv_layout == "HND",
+               True if enable_pdl is None else bool(enable_pdl), _status_arg(append_key.device))
+
+
+def apply_rope_and_append_paged_kv_cache(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
+                                         value: torch.Tensor, head_size: int, cos_sin_cache: torch.Tensor,
+                                         batch_indices: torch.Tensor, paged_kv_cache, kv_indices: torch.Tensor,
+                                         kv_indptr: torch.Tensor, kv_last_page_len: torch.Tensor,
+                                         is_neox: bool = True, kv_layout: str = "NHD",
+                                         llama_4_scaling_beta: float = 0.0,
+                                         original_max_position_embeddings: int = 1,
+                                         enable_pdl: Optional[bool] = None) -> None:
+    r"""Rope on q and k, the paged KV append of the rotated k and of v, and (when
+    `llama_4_scaling_beta` is nonzero) the llama-4 query scale, in one pass where the layout allows.
+
+    Equivalent to Devstral2Attention.forward's sequence (devstral2.py:163-179)::
+
+        apply_rope_with_cos_sin_cache_inplace(positions, query, key, head_size, cos_sin_cache, is_neox)
+        append_paged_kv_cache(key_heads, value_heads, batch_indices, positions, paged_kv_cache,
+                              kv_indices, kv_indptr, kv_last_page_len, kv_layout)
+        query *= (1 + beta * log1p(floor(positions.float() / original_max))).to(query.dtype)
+
+    with q scaled in place. k and v are read once; the rotated k is written back to `key` as well as
+    to the cache. A token whose position lies outside the cos/sin cache is neither rotated nor
+    appended (STATUS_ROPE_POS_OUT_OF_RANGE). `query`/`key` are ``(nnz, heads * head_size)`` or
+    ``(nnz, heads, head_size)`` views; `value` ``(nnz, num_kv_heads, head_size)`` or flat.
+    """
+    k_cache, v_cache = _unpack_paged_kv_cache(paged_kv_cache, kv_layout)
+    if cos_sin_cache.dtype != torch.float32:
+        raise ValueError("cos_sin_cache should be float32")
+    if cos_sin_cache.dim() != 2 or not cos_sin_cache.is_contiguous():
+        raise ValueError("cos_sin_cache must be a contiguous (max_seq_len, rotary_dim) tensor")
+    if positions.dtype not in _ID_DTYPES:
+        raise ValueError(f"positions must be int32 or int64, got {positions.dtype}")
+    if not (query.dtype == key.dtype == value.dtype):
+        raise ValueError("query, key and value must share one dtype")
+    _act_code(query)
+    rotary_dim = cos_sin_cache.shape[1]
+    if rotary_dim % 2 != 0 or rotary_dim > head_size:
+        raise ValueError(f"rotary_dim {rotary_dim} must be even and <= head_size {head_size}")
+    nnz = positions.shape[0]
+    if query.shape[0] != nnz or key.shape[0] != nnz or value.shape[0] != nnz or batch_indices.shape != (nnz,):
+        raise ValueError("positions, batch_indices, query, key and value must have the same number of tokens")
+    if llama_4_scaling_beta and original_max_position_embeddings <= 0:
+        raise ValueError("original_max_position_embeddings must be positive")
+    q = query.view(nnz, -1, head_size)
+    k = key.view(nnz, -1, head_size)
+    v = value.view(nnz, -1, head_size)
+    if v.shape != k.shape:
+        raise ValueError("key and value must have the same heads")
+    _check_paged(k_cache, v_cache, kv_indptr, kv_last_page_len, k.shape[1], head_size, kv_layout, query.dtype)
+    if nnz == 0:
+        return
+    _OP_ROPE_APPEND(q, k, v, cos_sin_cache, positions.contiguous(), _int32(batch_indices), k_cache, v_cache,
+                    _int32(kv_indices), _int32(kv_indptr), not is_neox, kv_layout == "HND",
+                    float(llama_4_scaling_beta or 0.0), int(original_max_position_embeddings),
+                    True if enable_pdl is None else bool(enable_pdl), _status_arg(query.device))
 
 
 # ------------------------------------------------------------------------------------------------

@@ -23,6 +23,7 @@ from .chain import ChainBuffers, ChainShape
 from .rope_cache import plain_cos_sin_cache
 
 __all__ = ["CHAIN_SHAPE", "norm_inputs", "silu_inputs", "rope_batch", "rope_inputs", "embed_inputs",
+           "paged_batch", "paged_batch_from_lengths", "PagedBatch", "rope_append_inputs",
            "chain_host_inputs", "chain_buffers", "RopeBatch"]
 
 CHAIN_SHAPE = ChainShape(hidden_size=12288, intermediate_size=28672, num_attention_heads=96,
@@ -80,6 +81,93 @@ def rope_inputs(device="cuda", seed: int = 2, num_q_heads: int = 32, num_kv_head
     k = _normal((T, num_kv_heads * head_dim), g, device, dtype)
     cache = plain_cos_sin_cache(head_dim, max_positions, theta).to(device)
     return b.positions.to(device), q, k, cache
+
+
+@dataclass
+class PagedBatch:
+    """One step's paged-KV metadata as ModelRunner / Devstral2Model.forward build it
+    (miniagentserve/engine/model_runner.py:31-66, models/devstral2/devstral2.py:283-290): decode rows
+    first (one new token each), then prompt chunks; every sequence's cache blocks come from a shared
+    pool, listed row by row in block_tables (batch, max_blocks) whose flattening is kv_indices."""
+
+    positions: torch.Tensor        # (T,) int32: each new token's position in its sequence
+    batch_indices: torch.Tensor    # (T,) int32
+    seq_lens: torch.Tensor         # (batch,) int32: cached + new tokens
+    block_tables: torch.Tensor     # (batch, max_blocks) int32
+    kv_indptr: torch.Tensor        # (batch + 1,) int32 = arange(batch + 1) * max_blocks
+    kv_last_page_len: torch.Tensor  # (batch,) int32 = (seq_lens - 1) % page_size + 1
+    num_pages: int
+    page_size: int
+
+    @property
+    def kv_indices(self) -> torch.Tensor:
+        return self.block_tables.flatten()
+
+    def to(self, device) -> "PagedBatch":
+        f = {k: (v.to(device) if torch.is_tensor(v) else v) for k, v in self.__dict__.items()}
+        return PagedBatch(**f)
+
+
+def paged_batch(seed: int = 6, num_decodes: int = 8, prompt_lens=(37, 64), max_cached: int = 300,
+                page_size: int = 16, spare_pages: int = 5) -> PagedBatch:
+    """A mixed step on the CPU: `num_decodes` decode rows with random cached lengths in
+    [1, max_cached], then prompt rows of `prompt_lens` new tokens after random cached prefixes.
+    Pages are a random permutation of a pool with `spare_pages` unused pages (plus the runner's
+    padding sink, page num_pages - 1); unused block-table slots point at the sink."""
+    g = torch.Generator().manual_seed(seed)
+    new = [1] * num_decodes + list(prompt_lens)
+    cached = torch.randint(1, max_cached + 1, (len(new),), generator=g).tolist()
+    if num_decodes < len(new):
+        for i in range(num_decodes, len(new)):
+            cached[i] = int(torch.randint(0, max_cached + 1, (1,), generator=g))
+    return paged_batch_from_lengths(cached, new, page_size, spare_pages, g)
+
+
+def paged_batch_from_lengths(cached, new, page_size: int = 16, spare_pages: int = 5,
+                             gen: torch.Generator | None = None) -> PagedBatch:
+    """Sequences of cached[b] tokens already in the cache and new[b] tokens this step, their blocks
+    a random permutation of the pool (see `paged_batch`)."""
+    g = torch.Generator().manual_seed(0) if gen is None else gen
+    cached, new = [int(c) for c in cached], [int(n) for n in new]
+    seq_lens = [c + n for c, n in zip(cached, new)]
+    blocks = [-(-L // page_size) for L in seq_lens]
+    max_blocks = max(blocks)
+    used = sum(blocks)
+    num_pages = used + spare_pages + 1
+    sink = num_pages - 1
+    perm = torch.randperm(num_pages - 1, generator=g)[:used].to(torch.int32)
+    table = torch.full((len(new), max_blocks), sink, dtype=torch.int32)
+    o = 0
+    for b, nb in enumerate(blocks):
+        table[b, :nb] = perm[o:o + nb]
+        o += nb
+    positions = torch.cat([torch.arange(c, c + n) for c, n in zip(cached, new)]).to(torch.int32)
+    batch_indices = torch.cat([torch.full((n,), b) for b, n in enumerate(new)]).to(torch.int32)
+    sl = torch.tensor(seq_lens, dtype=torch.int32)
+    return PagedBatch(positions=positions, batch_indices=batch_indices, seq_lens=sl, block_tables=table,
+                      kv_indptr=torch.arange(len(new) + 1, dtype=torch.int32) * max_blocks,
+                      kv_last_page_len=(sl - 1) % page_size + 1, num_pages=num_pages, page_size=page_size)
+
+
+def rope_append_inputs(device="cuda", seed: int = 2, num_q_heads: int = 32, num_kv_heads: int = 8,
+                       head_dim: int = 128, page_size: int = 16, max_positions: int = 131072, theta: float = 1e9,
+                       dtype=torch.bfloat16):
+    """Configuration 3's ragged batch (64 sequences of U[1, 1024] new tokens after random cached
+    prefixes) as one prefill step over a paged cache: (PagedBatch on device, qkv [T, (Hq+2Hkv)*D],
+    cos|sin cache, k_cache, v_cache [pages, page_size, Hkv, D])."""
+    rb = rope_batch(seed)
+    starts = torch.cumsum(rb.seq_lens, 0) - rb.seq_lens
+    cached = rb.positions[starts.long()].tolist()
+    b = paged_batch_from_lengths(cached, rb.seq_lens.tolist(), page_size, 5, torch.Generator().manual_seed(seed))
+    assert torch.equal(b.positions, rb.positions)
+    T = b.positions.shape[0]
+    g = _gen(device, seed)
+    qkv = _normal((T, (num_q_heads + 2 * num_kv_heads) * head_dim), g, device, dtype)
+    cache = plain_cos_sin_cache(head_dim, max_positions, theta).to(device)
+    shape = (b.num_pages, page_size, num_kv_heads, head_dim)
+    k_cache = torch.zeros(shape, dtype=dtype, device=device)
+    v_cache = torch.zeros(shape, dtype=dtype, device=device)
+    return b.to(device), qkv, cache, k_cache, v_cache
 
 
 def embed_inputs(device="cuda", seed: int = 3, vocab: int = 131072, hidden: int = 5120, tokens: int = 16384,

@@ -64,6 +64,12 @@ _SIGS = {
     "orc_rope_cos_sin_cache_q_scale_inplace": (
         _i32, [_vp, _i32, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _f32, _i64,
                _i32, _vp]),
+    "orc_append_paged_kv_cache": (
+        _i32, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _i64, _i64, _i64,
+               _i64, _i64, _i64, _i64, _i64, _vp]),
+    "orc_rope_append_paged_kv_cache": (
+        _i32, [_vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _i64,
+               _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _f32, _i64, _i32, _vp]),
     "orc_embedding_gather": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
     "orc_embedding_gather_fill_placeholders": (
         _i32, [_vp, _vp, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _vp]),
@@ -186,6 +192,63 @@ def apply_rope_and_llama4_query_scale_inplace(positions: torch.Tensor, query: to
         q.shape[1], k.shape[1], head_size, cache.shape[1], cache.shape[0], q.stride(0), q.stride(1), k.stride(0),
         k.stride(1), int(bool(is_neox)), float(beta), int(original_max_position_embeddings), _ACT[q.dtype],
         ctypes.byref(st)), "rope_q_scale")
+    return st.value
+
+
+def _paged(k_cache: torch.Tensor, v_cache: torch.Tensor, kv_layout: str):
+    """(num_pages, page_size, stride_page, stride_entry, stride_head) of a 4-D NHD / HND cache."""
+    if k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride():
+        raise ValueError("oracle: k and v caches must share shape and strides")
+    if kv_layout == "NHD":
+        return k_cache.shape[0], k_cache.shape[1], k_cache.stride(0), k_cache.stride(1), k_cache.stride(2)
+    return k_cache.shape[0], k_cache.shape[2], k_cache.stride(0), k_cache.stride(2), k_cache.stride(1)
+
+
+def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor, batch_indices: torch.Tensor,
+                          positions: torch.Tensor, paged_kv_cache, kv_indices: torch.Tensor,
+                          kv_indptr: torch.Tensor, kv_layout: str = "NHD") -> int:
+    """Appends (T, Hkv, D) k/v rows to the CPU caches in place; returns the status bits (8 = a slot
+    out of range)."""
+    k_cache, v_cache = paged_kv_cache
+    for n, t in (("append_key", append_key), ("append_value", append_value), ("batch_indices", batch_indices),
+                 ("positions", positions), ("k_cache", k_cache), ("v_cache", v_cache),
+                 ("kv_indices", kv_indices), ("kv_indptr", kv_indptr)):
+        _cpu(t, n)
+    bi, ki, kp = (x.to(torch.int32).contiguous() for x in (batch_indices, kv_indices, kv_indptr))
+    pos = positions.contiguous()
+    P, S, sp, se, sh = _paged(k_cache, v_cache, kv_layout)
+    st = ctypes.c_int32(0)
+    _ok(lib().orc_append_paged_kv_cache(
+        append_key.data_ptr(), append_value.data_ptr(), bi.data_ptr(), pos.data_ptr(), _IDS[pos.dtype],
+        k_cache.data_ptr(), v_cache.data_ptr(), P, S, sp, se, sh, ki.data_ptr(), ki.numel(), kp.data_ptr(),
+        kp.numel() - 1, append_key.shape[0], append_key.shape[1], append_key.shape[2], append_key.stride(0),
+        append_key.stride(1), append_value.stride(0), append_value.stride(1), ctypes.byref(st)), "append")
+    return st.value
+
+
+def rope_append_paged_kv_cache(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
+                               value: torch.Tensor, head_size: int, cos_sin_cache: torch.Tensor,
+                               batch_indices: torch.Tensor, paged_kv_cache, kv_indices: torch.Tensor,
+                               kv_indptr: torch.Tensor, is_neox: bool = True, kv_layout: str = "NHD",
+                               beta: float = 0.0, original_max_position_embeddings: int = 1) -> int:
+    """Rope on CPU q/k in place, the paged append of k and v, then (beta != 0) the llama-4 query scale.
+    query/key: (T, H*D) or (T, H, D) views; value (T, Hkv, D). Returns the status bits."""
+    k_cache, v_cache = paged_kv_cache
+    cache = cos_sin_cache.contiguous()
+    T = query.shape[0]
+    q = query.view(T, -1, head_size)
+    k = key.view(T, -1, head_size)
+    v = value.view(T, -1, head_size)
+    bi, ki, kp = (x.to(torch.int32).contiguous() for x in (batch_indices, kv_indices, kv_indptr))
+    pos = positions.contiguous()
+    P, S, sp, se, sh = _paged(k_cache, v_cache, kv_layout)
+    st = ctypes.c_int32(0)
+    _ok(lib().orc_rope_append_paged_kv_cache(
+        pos.data_ptr(), _IDS[pos.dtype], q.data_ptr(), k.data_ptr(), v.data_ptr(), cache.data_ptr(), bi.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr(), P, S, sp, se, sh, ki.data_ptr(), ki.numel(), kp.data_ptr(),
+        kp.numel() - 1, T, q.shape[1], k.shape[1], head_size, cache.shape[1], cache.shape[0], q.stride(0),
+        q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1), int(bool(is_neox)), float(beta),
+        int(original_max_position_embeddings), _ACT[q.dtype], ctypes.byref(st)), "rope_append")
     return st.value
 
 

@@ -310,6 +310,103 @@ int orc_rope_cos_sin_cache_q_scale_inplace(const void* positions, int positions_
 }
 
 /* ---------------------------------------------------------------------------------------------
+ * Paged KV append. FI/data/include/flashinfer/page.cuh:259-284 (kernel) with the element offsets of
+ * :161-165: token t of sequence b = batch_indices[t] at position p goes to
+ *   flat = kv_indptr[b] * page_size + p, page = kv_indices[flat / page_size], entry = flat % page_size
+ * and k_cache[page*stride_page + entry*stride_entry + h*stride_head + f] = k[t, h, f] (same for v),
+ * a byte copy. Indices are checked here (the reference kernel trusts them): a batch index outside
+ * [0, batch_size), a negative position, flat / page_size outside kv_indices or a page id outside
+ * [0, num_pages) skips the token and sets bit 8 of *status. pos_limit > 0 (used by the fused form
+ * below) skips tokens at positions outside [0, pos_limit) without flagging them.
+ * --------------------------------------------------------------------------------------------- */
+static int append_impl(const void* key, const void* value, const int32_t* batch_indices, const void* positions,
+                       int positions_dtype, void* k_cache, void* v_cache, int64_t num_pages, int64_t page_size,
+                       int64_t stride_page, int64_t stride_entry, int64_t stride_head, const int32_t* kv_indices,
+                       int64_t num_indices, const int32_t* kv_indptr, int64_t batch_size, int64_t num_tokens,
+                       int64_t num_kv_heads, int64_t head_size, int64_t k_stride_token, int64_t k_stride_head,
+                       int64_t v_stride_token, int64_t v_stride_head, int64_t pos_limit, int32_t* status) {
+  if (num_tokens < 0 || num_kv_heads < 0 || head_size <= 0 || page_size <= 0) return -1;
+  int32_t flags = 0;
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    const int64_t p = positions_dtype == ORC_INT64 ? ((const int64_t*)positions)[t]
+                                                   : (int64_t)((const int32_t*)positions)[t];
+    if (pos_limit > 0 && (p < 0 || p >= pos_limit)) continue;
+    const int64_t b = batch_indices[t];
+    if (b < 0 || b >= batch_size || p < 0) { flags |= 8; continue; }
+    const int64_t flat = (int64_t)kv_indptr[b] * page_size + p;
+    const int64_t page_iter = flat / page_size, entry = flat % page_size;
+    if (flat < 0 || page_iter >= num_indices) { flags |= 8; continue; }
+    const int64_t page = kv_indices[page_iter];
+    if (page < 0 || page >= num_pages) { flags |= 8; continue; }
+    for (int64_t h = 0; h < num_kv_heads; ++h) {
+      const int64_t dst = page * stride_page + entry * stride_entry + h * stride_head;
+      memcpy((uint16_t*)k_cache + dst, (const uint16_t*)key + t * k_stride_token + h * k_stride_head,
+             (size_t)head_size * 2);
+      memcpy((uint16_t*)v_cache + dst, (const uint16_t*)value + t * v_stride_token + h * v_stride_head,
+             (size_t)head_size * 2);
+    }
+  }
+  if (status) *status |= flags;
+  return 0;
+}
+
+int orc_append_paged_kv_cache(const void* key, const void* value, const int32_t* batch_indices,
+                              const void* positions, int positions_dtype, void* k_cache, void* v_cache,
+                              int64_t num_pages, int64_t page_size, int64_t stride_page, int64_t stride_entry,
+                              int64_t stride_head, const int32_t* kv_indices, int64_t num_indices,
+                              const int32_t* kv_indptr, int64_t batch_size, int64_t num_tokens,
+                              int64_t num_kv_heads, int64_t head_size, int64_t k_stride_token,
+                              int64_t k_stride_head, int64_t v_stride_token, int64_t v_stride_head,
+                              int32_t* status) {
+  return append_impl(key, value, batch_indices, positions, positions_dtype, k_cache, v_cache, num_pages,
+                     page_size, stride_page, stride_entry, stride_head, kv_indices, num_indices, kv_indptr,
+                     batch_size, num_tokens, num_kv_heads, head_size, k_stride_token, k_stride_head,
+                     v_stride_token, v_stride_head, 0, status);
+}
+
+/* Devstral2Attention.forward's sequence (devstral2.py:163-179): rope on q and k, the paged append of
+ * the rotated k and of v, then (beta != 0) the llama-4 query scale. A token whose position is
+ * outside [0, max_positions) is neither rotated nor appended (bit 2 of *status). */
+int orc_rope_append_paged_kv_cache(const void* positions, int positions_dtype, void* query, void* key,
+                                   const void* value, const float* cache, const int32_t* batch_indices,
+                                   void* k_cache, void* v_cache, int64_t num_pages, int64_t page_size,
+                                   int64_t stride_page, int64_t stride_entry, int64_t stride_head,
+                                   const int32_t* kv_indices, int64_t num_indices, const int32_t* kv_indptr,
+                                   int64_t batch_size, int64_t num_tokens, int64_t num_q_heads,
+                                   int64_t num_kv_heads, int64_t head_size, int64_t rotary_dim,
+                                   int64_t max_positions, int64_t q_stride_token, int64_t q_stride_head,
+                                   int64_t k_stride_token, int64_t k_stride_head, int64_t v_stride_token,
+                                   int64_t v_stride_head, int is_neox, float beta, int64_t original_max,
+                                   int dtype, int32_t* status) {
+  int rc = orc_rope_cos_sin_cache_inplace(positions, positions_dtype, query, key, cache, num_tokens, num_q_heads,
+                                          num_kv_heads, head_size, rotary_dim, max_positions, q_stride_token,
+                                          q_stride_head, k_stride_token, k_stride_head, is_neox, dtype, status);
+  if (rc != 0) return rc;
+  if (max_positions > 0) {
+    rc = append_impl(key, value, batch_indices, positions, positions_dtype, k_cache, v_cache, num_pages, page_size,
+                     stride_page, stride_entry, stride_head, kv_indices, num_indices, kv_indptr, batch_size,
+                     num_tokens, num_kv_heads, head_size, k_stride_token, k_stride_head, v_stride_token,
+                     v_stride_head, max_positions, status);
+    if (rc != 0) return rc;
+  }
+  if (beta == 0.0f) return 0;
+  if (original_max <= 0) return -1;
+  /* the query scale on the rotated q (k untouched: a second rope pass is not wanted) */
+  const float inv_orig = 1.0f / (float)original_max;
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    const int64_t pos = positions_dtype == ORC_INT64 ? ((const int64_t*)positions)[t]
+                                                     : (int64_t)((const int32_t*)positions)[t];
+    if (pos < 0 || pos >= max_positions) continue;
+    const float sc = llama4_q_scale(pos, beta, inv_orig, dtype);
+    for (int64_t h = 0; h < num_q_heads; ++h) {
+      uint16_t* p = (uint16_t*)query + t * q_stride_token + h * q_stride_head;
+      for (int64_t i = 0; i < head_size; ++i) p[i] = to_act(ld_act(&p[i], dtype) * sc, dtype);
+    }
+  }
+  return 0;
+}
+
+/* ---------------------------------------------------------------------------------------------
  * Token-embedding gather: out[t] = table[ids[t]], a byte copy (torch.nn.functional.embedding).
  * Out-of-range ids give a zero row and set bit 1 of *status.
  * --------------------------------------------------------------------------------------------- */

@@ -5,8 +5,10 @@
 mini-agent-serve computes RMSNorm, SiLU-and-mul and rope through flashinfer (imports at
 miniagentserve/models/devstral2/devstral2.py:18-23). This script calls those same functions with the
 arguments the reference's call sites pass -- fused_add_rmsnorm (devstral2.py:305-307),
-fused_add_rmsnorm_quant (:241-252), silu_and_mul (:224), apply_rope_with_cos_sin_cache_inplace on
-strided q/k views of one qkv row (:158-166) -- on small seeded inputs, and saves inputs and outputs
+fused_add_rmsnorm_quant (:241-252), silu_and_mul (:224) and the compiled quantize_fp8 after it
+(:93-95), apply_rope_with_cos_sin_cache_inplace on strided q/k views of one qkv row (:158-166),
+append_paged_kv_cache with the runner's page-table metadata (:170-173, :289-290) and the llama-4
+query scale (:175-179) -- on small seeded inputs, and saves inputs and outputs
 (bf16/fp16 as int16 bit patterns, e4m3 as uint8) to flashinfer_golden.npz. The CPU tests pin the
 oracle against these outputs; nothing in the product imports flashinfer.
 """
@@ -169,6 +171,76 @@ def main(out_dir: Path) -> None:
                            f"rope_{name}_dims": np.array([Hq, Hkv, D, int(neox)], dtype=np.int64)})
     except Exception:
         failures.append("apply_rope_with_cos_sin_cache_inplace: " + traceback.format_exc(limit=2))
+
+    # ---- append_paged_kv_cache, alone and after rope (+ llama-4 query scale) ------------------------
+    # Metadata as ModelRunner / Devstral2Model.forward build it (devstral2.py:283-290): decode rows
+    # first, then prompt rows; kv_indices = block_tables.flatten(), kv_indptr = arange(batch+1) *
+    # max_blocks, kv_last_page_len = (seq_lens - 1) % page_size + 1; pages drawn from a shared pool.
+    try:
+        from flashinfer.page import append_paged_kv_cache
+        from flashinfer.rope import apply_rope_with_cos_sin_cache_inplace
+
+        def paged_meta(new, page_size):
+            cached = torch.randint(0, 200, (len(new),), generator=g).tolist()
+            seq_lens = [c + n for c, n in zip(cached, new)]
+            blocks = [-(-L // page_size) for L in seq_lens]
+            mb, used = max(blocks), sum(blocks)
+            num_pages = used + 4
+            perm = torch.randperm(num_pages - 1, generator=g)[:used].to(torch.int32)
+            table = torch.full((len(new), mb), num_pages - 1, dtype=torch.int32)
+            o = 0
+            for b_, nb in enumerate(blocks):
+                table[b_, :nb] = perm[o:o + nb]
+                o += nb
+            pos = torch.cat([torch.arange(c, c + n) for c, n in zip(cached, new)]).to(torch.int32)
+            bi = torch.cat([torch.full((n,), b_) for b_, n in enumerate(new)]).to(torch.int32)
+            sl = torch.tensor(seq_lens, dtype=torch.int32)
+            indptr = torch.arange(len(new) + 1, dtype=torch.int32) * mb
+            return pos, bi, table, indptr, (sl - 1) % page_size + 1, num_pages
+
+        for name, new, page_size, layout, H, D in (("anhd", [1, 1, 1, 1, 9, 17], 16, "NHD", 8, 128),
+                                                   ("ahnd", [1, 1, 5, 30], 16, "HND", 2, 64),
+                                                   ("ap1", [1, 1, 3], 1, "NHD", 2, 64)):
+            pos, bi, table, indptr, last, num_pages = paged_meta(new, page_size)
+            T = pos.shape[0]
+            k = rnd(T, H, D)
+            v = rnd(T, H, D)
+            shape = (num_pages, H, page_size, D) if layout == "HND" else (num_pages, page_size, H, D)
+            kc, vc = rnd(*shape), rnd(*shape)
+            kc_d, vc_d = kc.to(dev), vc.to(dev)
+            append_paged_kv_cache(k.to(dev), v.to(dev), bi.to(dev), pos.to(dev), (kc_d, vc_d),
+                                  table.flatten().to(dev), indptr.to(dev), last.to(dev), kv_layout=layout)
+            torch.cuda.synchronize()
+            arrays.update({f"append_{name}_k": bits(k), f"append_{name}_v": bits(v), f"append_{name}_pos": pos.numpy(),
+                           f"append_{name}_bi": bi.numpy(), f"append_{name}_table": table.numpy(),
+                           f"append_{name}_indptr": indptr.numpy(), f"append_{name}_kc": bits(kc),
+                           f"append_{name}_vc": bits(vc), f"append_{name}_kcout": bits(kc_d),
+                           f"append_{name}_vcout": bits(vc_d), f"append_{name}_hnd": np.array(int(layout == "HND"))})
+
+        # Devstral2Attention.forward's sequence on one qkv row (devstral2.py:158-179)
+        Hq, H, D, P, beta, orig = 8, 2, 128, 4096, 0.1, 256
+        pos, bi, table, indptr, last, num_pages = paged_meta([1, 1, 1, 40], 16)
+        T = pos.shape[0]
+        qkv = rnd(T, (Hq + 2 * H) * D)
+        ang = torch.rand(P, D // 2, generator=g) * 6.283185307179586
+        cache = torch.cat([ang.cos(), ang.sin()], dim=-1).to(torch.float32)
+        kc, vc = rnd(num_pages, 16, H, D), rnd(num_pages, 16, H, D)
+        qkv_d, kc_d, vc_d, pos_d = qkv.to(dev), kc.to(dev), vc.to(dev), pos.to(dev)
+        q, k, v = qkv_d.split([Hq * D, H * D, H * D], dim=-1)
+        apply_rope_with_cos_sin_cache_inplace(pos_d, q, k, D, cache.to(dev), is_neox=True)
+        append_paged_kv_cache(k.unflatten(-1, (-1, D)), v.unflatten(-1, (-1, D)), bi.to(dev), pos_d, (kc_d, vc_d),
+                              table.flatten().to(dev), indptr.to(dev), last.to(dev), kv_layout="NHD")
+        scale = 1 + beta * torch.log1p(torch.floor(pos_d.float() / orig))
+        q_scaled = q.unflatten(-1, (-1, D)) * scale[:, None, None].to(q.dtype)
+        torch.cuda.synchronize()
+        arrays.update({"rapp_qkv": bits(qkv), "rapp_cache": cache.numpy(), "rapp_pos": pos.numpy(),
+                       "rapp_bi": bi.numpy(), "rapp_table": table.numpy(), "rapp_indptr": indptr.numpy(),
+                       "rapp_kc": bits(kc), "rapp_vc": bits(vc), "rapp_qkvout": bits(qkv_d),
+                       "rapp_qscaled": bits(q_scaled.flatten(1)), "rapp_kcout": bits(kc_d), "rapp_vcout": bits(vc_d),
+                       "rapp_dims": np.array([Hq, H, D], dtype=np.int64),
+                       "rapp_beta": np.array(beta, dtype=np.float32), "rapp_orig": np.array(orig)})
+    except Exception:
+        failures.append("append_paged_kv_cache: " + traceback.format_exc(limit=2))
 
     import flashinfer
     arrays["flashinfer_version"] = np.array(getattr(flashinfer, "__version__", "unknown"))

@@ -59,6 +59,16 @@ def test_python_constants_match_header():
     assert c["MAS_STATUS_EMBED_ID_OUT_OF_RANGE"] == _lib.STATUS_EMBED_ID_OUT_OF_RANGE
     assert c["MAS_STATUS_ROPE_POS_OUT_OF_RANGE"] == _lib.STATUS_ROPE_POS_OUT_OF_RANGE
     assert c["MAS_STATUS_COPY_TIMEOUT"] == _lib.STATUS_COPY_TIMEOUT
+    assert c["MAS_STATUS_KV_SLOT_OUT_OF_RANGE"] == _lib.STATUS_KV_SLOT_OUT_OF_RANGE
+
+
+def test_paged_kv_struct_layout_matches_header():
+    """struct MasPagedKVCache: two pointers, five int64, pointer, int64, pointer, int64 (88 bytes)."""
+    text = HEADER.read_text()
+    body = re.search(r"typedef struct MasPagedKVCache \{(.*?)\} MasPagedKVCache;", text, re.S).group(1)
+    fields = re.findall(r"(\w+);", body)
+    assert fields == [f for f, _ in _lib.PagedKVCache._fields_]
+    assert ctypes.sizeof(_lib.PagedKVCache) == 88
 
 
 def test_version_and_status_strings():
@@ -71,6 +81,12 @@ def test_version_and_status_strings():
 
 L = _lib.lib
 P = 0x1000  # a non-null pointer value; argument checks reject before any dereference or CUDA call
+
+
+def _kv(page_size=16):
+    c = _lib.PagedKVCache(k_cache=P, v_cache=P, num_pages=4, page_size=page_size, stride_page=16 * 64,
+                          stride_entry=64, stride_head=64, kv_indices=P, num_indices=4, kv_indptr=P, batch_size=1)
+    return ctypes.byref(c)
 
 
 @pytest.mark.parametrize("call,code", [
@@ -92,6 +108,20 @@ P = 0x1000  # a non-null pointer value; argument checks reject before any derefe
     (lambda: L.mas_embedding_gather(P, P, P, 6, 2, 8, 10, 8, 8, 2, None, 0, None), -2),
     (lambda: L.mas_embedding_gather(P, P, P, 4, 2, 8, 10, 4, 8, 2, None, 0, None), -1),
     (lambda: L.mas_embedding_gather(P, None, P, 4, 2, 8, 10, 8, 8, 2, None, 0, None), -1),
+    (lambda: L.mas_append_paged_kv_cache(P, P, P, P, 4, None, 2, 1, 64, 64, 64, 64, 64, 0, None, 0, None), -1),
+    (lambda: L.mas_append_paged_kv_cache(P, P, P, P, 4, _kv(page_size=0), 2, 1, 64, 64, 64, 64, 64, 0, None, 0,
+                                         None), -1),
+    (lambda: L.mas_append_paged_kv_cache(P, P, P, P, 4, _kv(), 2, 1, 64, 64, 64, 64, 64, 3, None, 0, None), -2),
+    (lambda: L.mas_append_paged_kv_cache(P, P, P, P, 9, _kv(), 2, 1, 64, 64, 64, 64, 64, 0, None, 0, None), -2),
+    (lambda: L.mas_append_paged_kv_cache(P, P, None, P, 4, _kv(), 2, 1, 64, 64, 64, 64, 64, 0, None, 0, None), -1),
+    (lambda: L.mas_rope_append_paged_kv_cache(P, 4, P, P, P, P, P, None, 2, 2, 1, 64, 64, 10, 0, 0, 0, 0, 0, 0, 1,
+                                              0.0, 1, 0, None, 0, None), -1),
+    (lambda: L.mas_rope_append_paged_kv_cache(P, 4, P, P, None, P, P, _kv(), 2, 2, 1, 64, 64, 10, 0, 0, 0, 0, 0, 0,
+                                              1, 0.0, 1, 0, None, 0, None), -1),
+    (lambda: L.mas_rope_append_paged_kv_cache(P, 4, P, P, P, P, P, _kv(), 2, 2, 1, 64, 65, 10, 0, 0, 0, 0, 0, 0, 1,
+                                              0.0, 1, 0, None, 0, None), -3),
+    (lambda: L.mas_rope_append_paged_kv_cache(P, 4, P, P, P, P, P, _kv(), 2, 2, 1, 64, 64, 10, 0, 0, 0, 0, 0, 0, 1,
+                                              0.5, 0, 0, None, 0, None), -1),
 ])
 def test_argument_checks_reject_before_launch(call, code):
     assert call() == code
@@ -104,6 +134,10 @@ def test_empty_batches_are_no_ops_without_a_device():
     assert L.mas_embedding_gather(None, None, None, 4, 0, 8, 10, 8, 8, 2, None, 0, None) == 0
     assert L.mas_rope_cos_sin_cache_inplace(None, 4, None, None, None, 0, 2, 1, 128, 128, 10, 0, 0, 0, 0, 1, 0,
                                             None, 0, None) == 0
+    assert L.mas_append_paged_kv_cache(None, None, None, None, 4, _kv(), 0, 1, 64, 64, 64, 64, 64, 0, None, 0,
+                                       None) == 0
+    assert L.mas_rope_append_paged_kv_cache(None, 4, None, None, None, None, None, _kv(), 0, 2, 1, 64, 64, 10, 0, 0,
+                                            0, 0, 0, 0, 1, 0.0, 1, 0, None, 0, None) == 0
 
 
 def test_valid_call_without_gpu_reports_no_device():

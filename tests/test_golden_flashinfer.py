@@ -98,3 +98,40 @@ def test_rope_matches_flashinfer(name):
     if name.startswith("rcancel"):
         # the evaluation order is pinned: every element, cancelling ones included, is identical
         assert stats["max_ulp"] == 0, stats
+
+
+def _i(a) -> torch.Tensor:
+    return torch.from_numpy(np.asarray(a))
+
+
+@pytest.mark.parametrize("name", _cases("append"))
+def test_append_matches_flashinfer(name):
+    """flashinfer.page.append_paged_kv_cache with the runner's metadata: the oracle's copy is exact."""
+    g = lambda k: Z[f"append_{name}_{k}"]  # noqa: E731
+    k, v = _t(g("k"), torch.bfloat16), _t(g("v"), torch.bfloat16)
+    kc, vc = _t(g("kc"), torch.bfloat16).clone(), _t(g("vc"), torch.bfloat16).clone()
+    st = oracle.append_paged_kv_cache(k, v, _i(g("bi")), _i(g("pos")), (kc, vc), _i(g("table")).flatten(),
+                                      _i(g("indptr")), kv_layout="HND" if int(g("hnd")) else "NHD")
+    assert st == 0
+    assert_bits_equal(kc, _t(g("kcout"), torch.bfloat16), f"{name} k cache")
+    assert_bits_equal(vc, _t(g("vcout"), torch.bfloat16), f"{name} v cache")
+
+
+@pytest.mark.skipif("rapp_qkv" not in Z.files, reason="fixture predates the rope + append case")
+def test_rope_append_q_scale_matches_reference_sequence():
+    """Rope -> append -> llama-4 query scale as Devstral2Attention.forward runs them (flashinfer +
+    eager torch on a B200) against the oracle's fused form: k/v caches and k within 1 ulp (exact
+    where the rotated k agrees), v untouched, q scaled within 1 ulp."""
+    Hq, H, D = (int(x) for x in Z["rapp_dims"])
+    qkv = _t(Z["rapp_qkv"], torch.bfloat16).clone()
+    kc, vc = _t(Z["rapp_kc"], torch.bfloat16).clone(), _t(Z["rapp_vc"], torch.bfloat16).clone()
+    st = oracle.rope_append_paged_kv_cache(
+        _i(Z["rapp_pos"]), qkv[:, : Hq * D], qkv[:, Hq * D: (Hq + H) * D], qkv[:, (Hq + H) * D:], D,
+        _i(Z["rapp_cache"]), _i(Z["rapp_bi"]), (kc, vc), _i(Z["rapp_table"]).flatten(), _i(Z["rapp_indptr"]),
+        beta=float(Z["rapp_beta"]), original_max_position_embeddings=int(Z["rapp_orig"]))
+    assert st == 0
+    ref = _t(Z["rapp_qkvout"], torch.bfloat16)
+    assert_ulp(qkv[:, Hq * D:], ref[:, Hq * D:], what="k rotated, v untouched")
+    assert_ulp(qkv[:, : Hq * D], _t(Z["rapp_qscaled"], torch.bfloat16), what="q rotated and scaled")
+    assert_ulp(kc, _t(Z["rapp_kcout"], torch.bfloat16), what="k cache")
+    assert_bits_equal(vc, _t(Z["rapp_vcout"], torch.bfloat16), "v cache")

@@ -207,3 +207,88 @@ def test_embedding_fill_placeholders_matches_reference_expression():
     bad = torch.tensor([-6, 3], dtype=torch.int64)  # row 5 of a 5-entry last_tokens
     out, st = oracle.embedding_fill_placeholders(bad, table, last_tokens)
     assert st == 1 and torch.count_nonzero(out[0].float()) == 0 and int(bad[0]) == -6
+
+
+def _append_loop(k, v, bi, pos, k_cache, v_cache, kv_indices, kv_indptr, page_size, hnd=False):
+    """flashinfer's append kernel (page.cuh:259-284) as a plain loop, no index checks."""
+    for i in range(k.shape[0]):
+        flat = int(kv_indptr[int(bi[i])]) * page_size + int(pos[i])
+        page, entry = int(kv_indices[flat // page_size]), flat % page_size
+        if hnd:
+            k_cache[page, :, entry] = k[i]
+            v_cache[page, :, entry] = v[i]
+        else:
+            k_cache[page, entry] = k[i]
+            v_cache[page, entry] = v[i]
+
+
+@pytest.mark.parametrize("hnd,pdt", [(False, torch.int32), (True, torch.int64)])
+def test_append_paged_kv_matches_formula(hnd, pdt):
+    from mas_b200 import workloads
+    b = workloads.paged_batch(seed=11, page_size=16)
+    T, H, D = b.positions.shape[0], 2, 64
+    g = torch.Generator().manual_seed(12)
+    qkv = torch.randn(T, (4 + 2 * H) * D, generator=g).to(torch.bfloat16)
+    k = qkv[:, 4 * D: (4 + H) * D].view(T, H, D)
+    v = qkv[:, (4 + H) * D:].view(T, H, D)
+    shape = (b.num_pages, H, b.page_size, D) if hnd else (b.num_pages, b.page_size, H, D)
+    kc, vc = torch.randn(shape, generator=g).to(torch.bfloat16), torch.randn(shape, generator=g).to(torch.bfloat16)
+    kw, vw = kc.clone(), vc.clone()
+    _append_loop(k, v, b.batch_indices, b.positions, kw, vw, b.kv_indices, b.kv_indptr, b.page_size, hnd)
+    st = oracle.append_paged_kv_cache(k, v, b.batch_indices, b.positions.to(pdt), (kc, vc), b.kv_indices,
+                                      b.kv_indptr, kv_layout="HND" if hnd else "NHD")
+    assert st == 0
+    assert_bits_equal(kc, kw, "k cache")
+    assert_bits_equal(vc, vw, "v cache")
+
+
+def test_append_paged_kv_out_of_range_slots_flagged():
+    from mas_b200 import workloads
+    b = workloads.paged_batch(seed=13, num_decodes=4, prompt_lens=(5,))
+    T, H, D = b.positions.shape[0], 1, 16
+    k = torch.randn(T, H, D).to(torch.bfloat16)
+    v = torch.randn(T, H, D).to(torch.bfloat16)
+    kc = torch.zeros(b.num_pages, b.page_size, H, D, dtype=torch.bfloat16)
+    vc = kc.clone()
+    bi = b.batch_indices.clone()
+    pos = b.positions.clone()
+    bi[0] = 99          # no such sequence
+    pos[1] = -3         # negative position
+    pos[2] = 10 ** 6    # past the page table
+    table = b.block_tables.clone()
+    table[int(bi[3]), int(pos[3]) // b.page_size] = b.num_pages + 7  # page id out of range
+    st = oracle.append_paged_kv_cache(k, v, bi, pos, (kc, vc), table.flatten(), b.kv_indptr)
+    assert st == 8
+    kw, vw = torch.zeros_like(kc), torch.zeros_like(vc)
+    keep = torch.arange(4, T)
+    _append_loop(k[keep], v[keep], bi[keep], pos[keep], kw, vw, table.flatten(), b.kv_indptr, b.page_size)
+    assert_bits_equal(kc, kw, "only in-range tokens appended")
+    assert_bits_equal(vc, vw, "only in-range tokens appended")
+
+
+def test_rope_append_is_rope_then_append_then_scale():
+    """The fused oracle equals its parts run in the reference's order (devstral2.py:163-179)."""
+    from mas_b200 import workloads
+    b = workloads.paged_batch(seed=14, page_size=8)
+    T, Hq, H, D, P = b.positions.shape[0], 4, 2, 64, 2048
+    g = torch.Generator().manual_seed(15)
+    qkv = torch.randn(T, (Hq + 2 * H) * D, generator=g).to(torch.bfloat16)
+    ang = torch.rand(P, D // 2, generator=g) * 6.283185307179586
+    cache = torch.cat([ang.cos(), ang.sin()], dim=-1).float()
+    kc = torch.zeros(b.num_pages, b.page_size, H, D, dtype=torch.bfloat16)
+    vc = kc.clone()
+    a = qkv.clone()
+    st = oracle.rope_append_paged_kv_cache(b.positions, a[:, : Hq * D], a[:, Hq * D: (Hq + H) * D],
+                                           a[:, (Hq + H) * D:], D, cache, b.batch_indices, (kc, vc), b.kv_indices,
+                                           b.kv_indptr, beta=0.1, original_max_position_embeddings=64)
+    assert st == 0
+    r = qkv.clone()
+    oracle.apply_rope_with_cos_sin_cache_inplace(b.positions, r[:, : Hq * D], r[:, Hq * D: (Hq + H) * D], D, cache)
+    kw, vw = torch.zeros_like(kc), torch.zeros_like(vc)
+    oracle.append_paged_kv_cache(r[:, Hq * D: (Hq + H) * D].view(T, H, D), r[:, (Hq + H) * D:].view(T, H, D),
+                                 b.batch_indices, b.positions, (kw, vw), b.kv_indices, b.kv_indptr)
+    scale = (1 + 0.1 * torch.log1p(torch.floor(b.positions.float() * (1.0 / 64)))).to(torch.bfloat16)
+    r[:, : Hq * D] = (r[:, : Hq * D].view(T, Hq, D) * scale[:, None, None]).view(T, -1)
+    assert_bits_equal(a, r, "q scaled, k rotated, v untouched")
+    assert_bits_equal(kc, kw, "k cache")
+    assert_bits_equal(vc, vw, "v cache")
