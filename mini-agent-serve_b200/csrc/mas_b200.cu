@@ -74,6 +74,10 @@ cudaError_t opt_in_norm_row() {
   if (e == cudaSuccess) e = opt_in_smem(norm_row_kernel<T, Q, 8>);
   if (e == cudaSuccess) e = opt_in_smem(norm_row_kernel<T, Q, 12>);
   if (e == cudaSuccess) e = opt_in_smem(norm_row_kernel<T, Q, 16>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_loop_kernel<T, Q, 4>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_loop_kernel<T, Q, 8>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_loop_kernel<T, Q, 12>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_loop_kernel<T, Q, 16>);
   return e;
 }
 
@@ -232,6 +236,39 @@ template <typename T, bool Q>
 int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int pdl) {
   const int H = a.H;
   static const bool use_ring = env_is("MAS_NORM_IMPL", "ring");
+  static const bool use_loop = env_is("MAS_NORM_IMPL", "loop");
+  if (fast_ok && H % 8 == 0 && use_loop) {
+    // Persistent row-group loop (norm_loop_kernel): S-stage ring, every thread a consumer.
+    static const int env_tpr = env_int("MAS_NORM_TPR", 0);
+    static const int env_cta = env_int("MAS_NORM_CTA_THREADS", 0);
+    static const int env_stages = env_int("MAS_NORM_STAGES", 0);
+    static const int env_ctas = env_int("MAS_NORM_CTAS_PER_SM", 0);
+    int tpr = H <= 3072 ? 32 : H <= 6144 ? 64 : H <= 16384 ? 128 : 256;
+    if (env_tpr > 0) tpr = env_tpr;
+    int cta = env_cta > 0 ? env_cta : std::max(128, tpr);
+    tpr = std::max(32, std::min(tpr, kNormRowMaxThreads)) / 32 * 32;
+    cta = std::max(tpr, std::min(cta, kNormRowMaxThreads)) / tpr * tpr;
+    const int rpc = cta / tpr;
+    const int vpt = (int)ceil_div(H / 8, tpr);
+    const int stages = std::max(2, std::min(8, env_stages > 0 ? env_stages : 3));
+    const size_t smem = norm_loop_smem_bytes(H, rpc, stages, (int)sizeof(T));
+    if (smem <= kMaxSmemPerCta && vpt <= 16) {
+      const void* fn = vpt <= 4 ? (const void*)norm_loop_kernel<T, Q, 4>
+                     : vpt <= 8 ? (const void*)norm_loop_kernel<T, Q, 8>
+                     : vpt <= 12 ? (const void*)norm_loop_kernel<T, Q, 12>
+                                 : (const void*)norm_loop_kernel<T, Q, 16>;
+      int ctas = resident_ctas(fn, cta, smem);
+      if (env_ctas > 0) ctas = std::min(ctas, env_ctas);
+      const int64_t ngroups = ceil_div(a.rows, rpc);
+      const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(ngroups, (int64_t)st.sm_count * std::max(1, ctas)));
+      a.stages = stages;
+      const dim3 g((unsigned)grid), b(cta);
+      if (vpt <= 4) return launch(norm_loop_kernel<T, Q, 4>, g, b, smem, stream, pdl, a, tpr, rpc);
+      if (vpt <= 8) return launch(norm_loop_kernel<T, Q, 8>, g, b, smem, stream, pdl, a, tpr, rpc);
+      if (vpt <= 12) return launch(norm_loop_kernel<T, Q, 12>, g, b, smem, stream, pdl, a, tpr, rpc);
+      return launch(norm_loop_kernel<T, Q, 16>, g, b, smem, stream, pdl, a, tpr, rpc);
+    }
+  }
   if (fast_ok && H % 8 == 0 && !use_ring) {
     // Row-block CTAs: threads per row grow with H (32 ... 256), 128 or 256 threads per CTA.
     static const int env_tpr = env_int("MAS_NORM_TPR", 0);
@@ -308,7 +345,7 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
                        int enable_pdl) {
   const uint32_t stage = rope_stage_bytes(r.Hq, r.Hkv, r.D, r.rd, 2, APPEND);
   static const int env_stages = env_int("MAS_ROPE_STAGES", 0);
-  const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
+  int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
   const size_t per_cta = rope_ring_smem_bytes(stage, stages, kRopeMaxTokensPerCta, APPEND);
   if (per_cta > kMaxSmemPerCta) return kNotLaunched;
   const void* fn = bf ? (i64 ? (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, true, APPEND>
@@ -325,6 +362,15 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
   grid = std::min<int64_t>(grid, r.T);
   r.tokens_per_cta = (int32_t)ceil_div(r.T, grid);
   grid = ceil_div(r.T, r.tokens_per_cta);
+  if (env_stages <= 0) {
+    // Deepen the ring into this CTA's share of the SM's shared memory (at most one stage per token):
+    // with few tokens per CTA the pipeline never reaches steady state, so the bytes in flight per
+    // SM are what the stages hold.
+    const size_t budget = kRingBytesPerSm / (size_t)ctas;
+    const size_t fixed = (size_t)r.tokens_per_cta * (APPEND ? 16 : 8);
+    const size_t fit = budget > fixed ? (budget - fixed) / (stage + 16) : 0;
+    stages = (int)std::max<size_t>(stages, std::min<size_t>({fit, 16, (size_t)r.tokens_per_cta}));
+  }
   r.stages = stages;
   const size_t smem = rope_ring_smem_bytes(stage, stages, r.tokens_per_cta, APPEND);
   const dim3 g((unsigned)grid), b(kRopeRingThreads);
@@ -510,8 +556,9 @@ static int silu_impl(void* out, const void* input, const float* scale, int64_t n
   const bool bf16 = dtype == MAS_DTYPE_BF16;
   if (vec && (quant || !use_ring)) {
     static const int env_rows = env_int("MAS_SILU_GRID_ROWS", 0);
-    const dim3 grid((unsigned)ceil_div(d / 8, kSiluThreads),
-                    (unsigned)std::min<int64_t>(num_tokens, env_rows > 0 ? env_rows : 65535));
+    // 16 row groups per SM: each thread walks a few rows, so CTA start-up is amortised without a tail
+    const int64_t rows = env_rows > 0 ? env_rows : 16 * (int64_t)st->sm_count;
+    const dim3 grid((unsigned)ceil_div(d / 8, kSiluThreads), (unsigned)std::min<int64_t>({num_tokens, rows, 65535}));
     const dim3 block(kSiluThreads);
     if (quant) {
       return bf16 ? launch(silu_mul_vec_kernel<__nv_bfloat16, true>, grid, block, 0, stream, enable_pdl, a)

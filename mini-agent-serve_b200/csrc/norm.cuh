@@ -332,6 +332,146 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
   pdl_launch_dependents();
 }
 
+// Persistent variant of the row-block kernel: grid = SMs x resident CTAs, CTA c handling row groups
+// c, c + grid, ... (rpc rows each, tpr threads per row). Thread 0 keeps S - 1 groups' bulk copies in
+// flight ahead of the one being computed, in an S-stage shared-memory ring (one mbarrier per stage);
+// the weight slice stays in registers for the CTA's lifetime. Each iteration ends with a CTA
+// barrier, after which the stage just consumed is refilled. No producer warp: every thread computes.
+__host__ __device__ inline size_t norm_loop_smem_bytes(int H, int rpc, int stages, int elem_bytes) {
+  return (size_t)stages * rpc * 2 * (size_t)H * (size_t)elem_bytes + (size_t)stages * 8 +
+         (size_t)(kNormRowMaxThreads / 32) * sizeof(float);
+}
+
+template <typename T, bool QUANT, int MAXV>
+__global__ void __launch_bounds__(kNormRowMaxThreads) norm_loop_kernel(const NormArgs a, int tpr, int rpc) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int H = a.H;
+  const int NV = H >> 3;
+  const int S = a.stages;
+  const uint32_t row_bytes = (uint32_t)H * (uint32_t)sizeof(T);
+  const size_t stage_bytes = (size_t)rpc * 2 * row_bytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  float* red = reinterpret_cast<float*>(bar + S);
+  const int tid = threadIdx.x;
+  const int rr = tid / tpr;
+  const int rt = tid - rr * tpr;
+  const int64_t ngroups = (a.rows + rpc - 1) / rpc;
+  const int64_t g0 = blockIdx.x, gstep = gridDim.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  T* const xb = static_cast<T*>(a.x);
+  T* const rb = static_cast<T*>(a.r);
+  auto issue = [&](int64_t g, int s) {
+    const int64_t row0 = g * rpc;
+    const int n = (int)min((int64_t)rpc, a.rows - row0);
+    unsigned char* st = smem + (size_t)s * stage_bytes;
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)n * 2 * row_bytes);
+    for (int i = 0; i < n; ++i) {
+      bulk_load(st + (size_t)i * 2 * row_bytes, xb + (row0 + i) * a.x_stride, row_bytes, &bar[s]);
+      bulk_load(st + (size_t)i * 2 * row_bytes + row_bytes, rb + (row0 + i) * a.r_stride, row_bytes, &bar[s]);
+    }
+  };
+  if (tid == 0) {
+    for (int k = 0; k < S - 1; ++k) {
+      const int64_t g = g0 + (int64_t)k * gstep;
+      if (g < ngroups) issue(g, k);
+    }
+  }
+  float inv_scale = 1.0f;
+  if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
+  Vec16 wv[MAXV];
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = rt + j * tpr;
+    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+  }
+
+  int k = 0;
+  bool timed_out = false;
+  for (int64_t g = g0; g < ngroups; g += gstep, ++k) {
+    const int s = k % S;
+    if (tid == 0) {
+      const int64_t gn = g + (int64_t)(S - 1) * gstep;  // refill the stage consumed last iteration
+      if (gn < ngroups) {
+        fence_proxy_async_smem();
+        issue(gn, (k + S - 1) % S);
+      }
+    }
+    const bool ok = mbar_wait_bounded(&bar[s], (uint32_t)(k / S) & 1u);
+    const int64_t row0 = g * rpc;
+    const bool active = rr < (int)min((int64_t)rpc, a.rows - row0);
+    const int64_t row = row0 + rr;
+    const unsigned char* sx = smem + (size_t)s * stage_bytes + (size_t)rr * 2 * row_bytes;
+    const unsigned char* sr = sx + row_bytes;
+    float ss = 0.f;
+    if (ok && active) {
+#pragma unroll
+      for (int j = 0; j < MAXV; ++j) {
+        const int v = rt + j * tpr;
+        if (v >= NV) break;
+        float xf[8], rf[8];
+        unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
+        unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xf[e] += rf[e];
+          ss += xf[e] * xf[e];
+        }
+        st_plain(rb + row * a.r_stride + (size_t)v * 8, pack8<T>(xf));
+      }
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    if (__syncthreads_or(!ok)) {
+      timed_out = true;
+      break;
+    }
+    if (active) {
+      float tot = 0.f;
+      const int w0 = (rr * tpr) >> 5, nw = tpr >> 5;
+      for (int w = 0; w < nw; ++w) tot += red[w0 + w];
+      const float rstd = rsqrtf(tot * (1.0f / (float)H) + a.eps);
+#pragma unroll
+      for (int j = 0; j < MAXV; ++j) {
+        const int v = rt + j * tpr;
+        if (v >= NV) break;
+        float xf[8], rf[8], wf[8];
+        unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
+        unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
+        unpack8<T>(wv[j], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xf[e] = (xf[e] + rf[e]) * rstd * wf[e];
+        if constexpr (QUANT) {
+          uint2 q;
+          q.x = (uint32_t)f2_to_e4m3x2(xf[0] * inv_scale, xf[1] * inv_scale) |
+                ((uint32_t)f2_to_e4m3x2(xf[2] * inv_scale, xf[3] * inv_scale) << 16);
+          q.y = (uint32_t)f2_to_e4m3x2(xf[4] * inv_scale, xf[5] * inv_scale) |
+                ((uint32_t)f2_to_e4m3x2(xf[6] * inv_scale, xf[7] * inv_scale) << 16);
+          *reinterpret_cast<uint2*>(a.out + row * a.out_stride + (size_t)v * 8) = q;
+        } else {
+          st_plain(xb + row * a.x_stride + (size_t)v * 8, pack8<T>(xf));
+        }
+      }
+    }
+    __syncthreads();  // stage s and red[] are free again
+  }
+  if (timed_out && tid == 0) {
+    // Iteration k's wait gave up: the fills of iterations k .. k + S - 1 may still be landing in this
+    // CTA's shared memory. Wait for each (bounded) before the CTA exits.
+    atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+    for (int m = 0; m < S; ++m) {
+      const int64_t gm = g0 + (int64_t)(k + m) * gstep;
+      if (gm < ngroups) (void)mbar_wait_bounded(&bar[(k + m) % S], (uint32_t)((k + m) / S) & 1u);
+    }
+  }
+  pdl_launch_dependents();
+}
+
 // Generic path: one CTA per row, scalar elements, any alignment.
 template <typename T, bool QUANT>
 __global__ void __launch_bounds__(256) norm_generic_kernel(const NormArgs a) {

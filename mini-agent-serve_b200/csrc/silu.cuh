@@ -125,12 +125,42 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
   pdl_launch_dependents();
 }
 
-// FP8Linear's activation quantisation of one silu output (rounded to the activation type first):
-// (act / scale) in fp32 with an IEEE quotient, clamped to +-448 and rounded to nearest even e4m3
-// (satfinite does the clamp; NaN stays NaN, as with a clamp that propagates it).
-__device__ __forceinline__ uint32_t quant4_e4m3(const float* act, float scale) {
-  return (uint32_t)f2_to_e4m3x2(__fdiv_rn(act[0], scale), __fdiv_rn(act[1], scale)) |
-         ((uint32_t)f2_to_e4m3x2(__fdiv_rn(act[2], scale), __fdiv_rn(act[3], scale)) << 16);
+// The fp32 quotient act / scale of FP8Linear's activation quantisation, without a divide
+// instruction: q0 = act * r with r = 1/scale (rounded once per thread), then one remainder step of
+// Markstein's FMA division (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990): rem = fma(-scale, q0, act) is exact and
+// fma(r, rem, q0) is the correctly rounded quotient. The step is applied where it can change the
+// e4m3 result, |q0| in [2^-12, 512): below, e4m3 rounds to a zero of the right sign; above, it
+// saturates. With this restriction the quotient equals the IEEE one on every bf16 and every fp16
+// activation, checked exhaustively on the CPU for 20,000 scales. `fast` is false when scale or r is
+// not a normal number; the IEEE divide is used then.
+struct QuantDiv {
+  float scale, r;
+  bool fast;
+  __device__ __forceinline__ float operator()(float x) const {
+    if (!fast) return __fdiv_rn(x, scale);
+    const float q0 = __fmul_rn(x, r);
+    const float q1 = __fmaf_rn(r, __fmaf_rn(-scale, q0, x), q0);
+    const float a = fabsf(q0);
+    return (a >= 0x1p-12f && a < 512.0f) ? q1 : q0;
+  }
+};
+
+__device__ __forceinline__ QuantDiv make_quant_div(float s) {
+  QuantDiv d;
+  d.scale = s;
+  d.r = __frcp_rn(s);
+  d.fast = fabsf(s) >= 0x1p-126f && fabsf(s) <= 0x1.fffffep127f && fabsf(d.r) >= 0x1p-126f &&
+           fabsf(d.r) <= 0x1.fffffep127f;
+  return d;
+}
+
+// FP8Linear's activation quantisation of four silu outputs (already rounded to the activation type):
+// (act / scale) in fp32, clamped to +-448 and rounded to nearest even e4m3 (satfinite does the
+// clamp; NaN stays NaN, as with a clamp that propagates it).
+__device__ __forceinline__ uint32_t quant4_e4m3(const float* act, const QuantDiv& div) {
+  return (uint32_t)f2_to_e4m3x2(div(act[0]), div(act[1])) |
+         ((uint32_t)f2_to_e4m3x2(div(act[2]), div(act[3])) << 16);
 }
 
 // Register variant (the default fast path): one 16-byte gate/up pair per thread and row, 32
@@ -142,8 +172,7 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
   pdl_wait();
   const int nvec = a.d >> 3;
   const int v = blockIdx.x * kSiluThreads + threadIdx.x;
-  float scale = 1.0f;
-  if constexpr (QUANT) scale = *a.scale;
+  const QuantDiv div = make_quant_div(QUANT ? *a.scale : 1.0f);
   if (v < nvec) {
     for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
       const T* g = static_cast<const T*>(a.in) + row * a.in_stride + (size_t)v * 8;
@@ -157,8 +186,8 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
       if constexpr (QUANT) {
         unpack8<T>(pack8<T>(y), y);  // the activation as the unfused op would have stored it
         uint2 q;
-        q.x = quant4_e4m3(y, scale);
-        q.y = quant4_e4m3(y + 4, scale);
+        q.x = quant4_e4m3(y, div);
+        q.y = quant4_e4m3(y + 4, div);
         *reinterpret_cast<uint2*>(static_cast<uint8_t*>(a.out) + row * a.out_stride + (size_t)v * 8) = q;
       } else {
         st_plain(static_cast<T*>(a.out) + row * a.out_stride + (size_t)v * 8, pack8<T>(y));
@@ -171,8 +200,7 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
 template <typename T, bool QUANT>
 __global__ void __launch_bounds__(kSiluThreads) silu_mul_generic_kernel(const SiluArgs a) {
   pdl_wait();
-  float scale = 1.0f;
-  if constexpr (QUANT) scale = *a.scale;
+  const QuantDiv div = make_quant_div(QUANT ? *a.scale : 1.0f);
   for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
     const uint16_t* g = static_cast<const uint16_t*>(a.in) + row * a.in_stride;
     const uint16_t* u = g + a.d;
@@ -180,7 +208,7 @@ __global__ void __launch_bounds__(kSiluThreads) silu_mul_generic_kernel(const Si
       const uint16_t act = Elem<T>::from_f(silu_f32(Elem<T>::to_f(g[i])) * Elem<T>::to_f(u[i]));
       if constexpr (QUANT) {
         static_cast<uint8_t*>(a.out)[row * a.out_stride + i] =
-            (uint8_t)(f2_to_e4m3x2(__fdiv_rn(Elem<T>::to_f(act), scale), 0.f) & 0xffu);
+            (uint8_t)(f2_to_e4m3x2(div(Elem<T>::to_f(act)), 0.f) & 0xffu);
       } else {
         static_cast<uint16_t*>(a.out)[row * a.out_stride + i] = act;
       }
