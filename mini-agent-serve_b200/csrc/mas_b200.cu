@@ -236,21 +236,26 @@ template <typename T, bool Q>
 int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int pdl) {
   const int H = a.H;
   static const bool use_ring = env_is("MAS_NORM_IMPL", "ring");
+  static const bool use_row = env_is("MAS_NORM_IMPL", "row");
   static const bool use_loop = env_is("MAS_NORM_IMPL", "loop");
-  if (fast_ok && H % 8 == 0 && use_loop) {
-    // Persistent row-group loop (norm_loop_kernel): S-stage ring, every thread a consumer.
+  // Default: the persistent loop up to H = 6144 (config 1's H = 5120 measured 26.6 us against 29.5
+  // for the row-block grid), the row-block grid above (H = 12288: 67 us against 73+ for the loop).
+  if (fast_ok && H % 8 == 0 && (use_loop || (!use_ring && !use_row && H <= 6144))) {
+    // Persistent row-group loop (norm_loop_kernel): S-stage ring, every thread a consumer. By
+    // default at most 4 vectors per thread (threads per row = H/32, rounded up to a warp), two rows
+    // per CTA and two stages, which leaves two CTAs per SM at H = 5120.
     static const int env_tpr = env_int("MAS_NORM_TPR", 0);
     static const int env_cta = env_int("MAS_NORM_CTA_THREADS", 0);
     static const int env_stages = env_int("MAS_NORM_STAGES", 0);
     static const int env_ctas = env_int("MAS_NORM_CTAS_PER_SM", 0);
-    int tpr = H <= 3072 ? 32 : H <= 6144 ? 64 : H <= 16384 ? 128 : 256;
+    int tpr = (int)ceil_div(ceil_div(H / 8, 4), 32) * 32;
     if (env_tpr > 0) tpr = env_tpr;
-    int cta = env_cta > 0 ? env_cta : std::max(128, tpr);
     tpr = std::max(32, std::min(tpr, kNormRowMaxThreads)) / 32 * 32;
+    int cta = env_cta > 0 ? env_cta : std::min(2 * tpr, kNormRowMaxThreads);
     cta = std::max(tpr, std::min(cta, kNormRowMaxThreads)) / tpr * tpr;
     const int rpc = cta / tpr;
     const int vpt = (int)ceil_div(H / 8, tpr);
-    const int stages = std::max(2, std::min(8, env_stages > 0 ? env_stages : 3));
+    const int stages = std::max(2, std::min(8, env_stages > 0 ? env_stages : 2));
     const size_t smem = norm_loop_smem_bytes(H, rpc, stages, (int)sizeof(T));
     if (smem <= kMaxSmemPerCta && vpt <= 16) {
       const void* fn = vpt <= 4 ? (const void*)norm_loop_kernel<T, Q, 4>
@@ -305,16 +310,21 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
     static const int env_stages = env_int("MAS_NORM_STAGES", 0);
     // Ring depth first (4 stages), then as many CTAs per SM as the ring budget, the thread limit and
     // the occupancy (registers) allow; budget left over deepens the ring (up to 8 stages).
+    // Consumer group g takes rows g, g + G, ... and stage s serves rows s, s + S, ...; with S a
+    // multiple of G the previous user of a stage is the same group, which keeps every parity wait
+    // on the stage's barriers within one phase (norm_tma_kernel relies on it). So S is rounded down
+    // to a multiple of G (G <= 4 <= 8 leaves at least G stages).
+    const auto multiple_of_groups = [groups](int st_) { return std::max(groups, st_ / groups * groups); };
     const void* fn = norm_tma_fn<T, Q>(vpt);
     int stages = env_stages > 0 ? env_stages : 4;
     if ((size_t)stages * stage > kRingBytesPerSm) stages = (int)std::max<size_t>(2, kRingBytesPerSm / stage);
-    stages = std::max(2, std::min(8, stages));
+    stages = multiple_of_groups(std::max(2, std::min(8, stages)));
     size_t smem = norm_tma_smem_bytes(H, stages, (int)sizeof(T));
     if (fn != nullptr && smem <= kMaxSmemPerCta) {
       int ctas = env_ctas > 0 ? env_ctas : (int)std::max<size_t>(1, kRingBytesPerSm / ((size_t)stages * stage));
       ctas = std::max(1, std::min({ctas, 2048 / nt, resident_ctas(fn, nt, smem)}));
       if (env_stages <= 0) {
-        const int deeper = (int)std::min<size_t>(8, kRingBytesPerSm / ((size_t)ctas * stage));
+        const int deeper = multiple_of_groups((int)std::min<size_t>(8, kRingBytesPerSm / ((size_t)ctas * stage)));
         if (deeper > stages && norm_tma_smem_bytes(H, deeper, (int)sizeof(T)) <= kMaxSmemPerCta) {
           stages = deeper;
           smem = norm_tma_smem_bytes(H, stages, (int)sizeof(T));
@@ -345,7 +355,7 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
                        int enable_pdl) {
   const uint32_t stage = rope_stage_bytes(r.Hq, r.Hkv, r.D, r.rd, 2, APPEND);
   static const int env_stages = env_int("MAS_ROPE_STAGES", 0);
-  int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
+  const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
   const size_t per_cta = rope_ring_smem_bytes(stage, stages, kRopeMaxTokensPerCta, APPEND);
   if (per_cta > kMaxSmemPerCta) return kNotLaunched;
   const void* fn = bf ? (i64 ? (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, true, APPEND>
@@ -362,15 +372,6 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
   grid = std::min<int64_t>(grid, r.T);
   r.tokens_per_cta = (int32_t)ceil_div(r.T, grid);
   grid = ceil_div(r.T, r.tokens_per_cta);
-  if (env_stages <= 0) {
-    // Deepen the ring into this CTA's share of the SM's shared memory (at most one stage per token):
-    // with few tokens per CTA the pipeline never reaches steady state, so the bytes in flight per
-    // SM are what the stages hold.
-    const size_t budget = kRingBytesPerSm / (size_t)ctas;
-    const size_t fixed = (size_t)r.tokens_per_cta * (APPEND ? 16 : 8);
-    const size_t fit = budget > fixed ? (budget - fixed) / (stage + 16) : 0;
-    stages = (int)std::max<size_t>(stages, std::min<size_t>({fit, 16, (size_t)r.tokens_per_cta}));
-  }
   r.stages = stages;
   const size_t smem = rope_ring_smem_bytes(stage, stages, r.tokens_per_cta, APPEND);
   const dim3 g((unsigned)grid), b(kRopeRingThreads);

@@ -90,6 +90,13 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
 
   const int64_t row0 = (int64_t)blockIdx.x * a.rows_per_cta;
   const int n = (int)min((int64_t)a.rows_per_cta, a.rows - row0);
+  // Stage s serves rows s, s + S, ...; group g consumes rows g, g + G, .... The parity waits below
+  // are exact only if a stage's previous row belonged to the same group, i.e. S % G == 0 (a group
+  // could otherwise reach a stage two phases early). The host guarantees it; refuse otherwise.
+  if (S % G != 0) {
+    if (tid == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+    return;
+  }
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {

@@ -361,6 +361,15 @@ def _unpack_paged_kv_cache(paged_kv_cache, kv_layout: str) -> tuple[torch.Tensor
     return k_cache, v_cache
 
 
+def _heads(t: torch.Tensor, head_size: int) -> torch.Tensor:
+    """(tokens, heads, head_size) view of a (tokens, heads * head_size) or 3-D tensor."""
+    if t.dim() == 3:
+        return t
+    if t.dim() != 2 or t.shape[-1] % head_size != 0:
+        raise ValueError(f"expected (tokens, heads * {head_size}) or (tokens, heads, {head_size}), got {tuple(t.shape)}")
+    return t.view(t.shape[0], t.shape[-1] // head_size, head_size)
+
+
 def _int32(t: torch.Tensor) -> torch.Tensor:
     return t if t.dtype == torch.int32 and t.is_contiguous() else t.int().contiguous()
 
@@ -453,9 +462,7 @@ def apply_rope_and_append_paged_kv_cache(positions: torch.Tensor, query: torch.T
         raise ValueError("positions, batch_indices, query, key and value must have the same number of tokens")
     if llama_4_scaling_beta and original_max_position_embeddings <= 0:
         raise ValueError("original_max_position_embeddings must be positive")
-    q = query.view(nnz, -1, head_size)
-    k = key.view(nnz, -1, head_size)
-    v = value.view(nnz, -1, head_size)
+    q, k, v = (_heads(t, head_size) for t in (query, key, value))
     if v.shape != k.shape:
         raise ValueError("key and value must have the same heads")
     _check_paged(k_cache, v_cache, kv_indptr, kv_last_page_len, k.shape[1], head_size, kv_layout, query.dtype)

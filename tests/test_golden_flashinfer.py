@@ -117,7 +117,6 @@ def test_append_matches_flashinfer(name):
     assert_bits_equal(vc, _t(g("vcout"), torch.bfloat16), f"{name} v cache")
 
 
-@pytest.mark.skipif("rapp_qkv" not in Z.files, reason="fixture predates the rope + append case")
 def test_rope_append_q_scale_matches_reference_sequence():
     """Rope -> append -> llama-4 query scale as Devstral2Attention.forward runs them (flashinfer +
     eager torch on a B200) against the oracle's fused form: k/v caches and k within 1 ulp (exact
