@@ -367,14 +367,16 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
                              : (neox ? (const void*)rope_ring_kernel<__half, int32_t, true, APPEND>
                                      : (const void*)rope_ring_kernel<__half, int32_t, false, APPEND>));
   int ctas = (int)std::max<size_t>(1, kRingBytesPerSm / per_cta);
-  ctas = std::min(ctas, resident_ctas(fn, kRopeRingThreads, per_cta));
+  static const int env_warps = env_int("MAS_ROPE_CONSUMER_WARPS", 0);
+  const int threads = 32 * (1 + std::max(1, std::min(kRopeMaxConsumerWarps, env_warps > 0 ? env_warps : kRopeConsumerWarps)));
+  ctas = std::min(ctas, resident_ctas(fn, threads, per_cta));
   int64_t grid = std::max<int64_t>((int64_t)st->sm_count * ctas, ceil_div(r.T, kRopeMaxTokensPerCta));
   grid = std::min<int64_t>(grid, r.T);
   r.tokens_per_cta = (int32_t)ceil_div(r.T, grid);
   grid = ceil_div(r.T, r.tokens_per_cta);
   r.stages = stages;
   const size_t smem = rope_ring_smem_bytes(stage, stages, r.tokens_per_cta, APPEND);
-  const dim3 g((unsigned)grid), b(kRopeRingThreads);
+  const dim3 g((unsigned)grid), b(threads);
   if (bf) {
     if (i64) return neox ? launch(rope_ring_kernel<__nv_bfloat16, int64_t, true, APPEND>, g, b, smem, stream, enable_pdl, r)
                          : launch(rope_ring_kernel<__nv_bfloat16, int64_t, false, APPEND>, g, b, smem, stream, enable_pdl, r);

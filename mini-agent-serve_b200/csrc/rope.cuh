@@ -188,8 +188,9 @@ struct RopeRingArgs {
   PagedKVArgs kv;
 };
 
-constexpr int kRopeConsumerWarps = 8;
-constexpr int kRopeRingThreads = 32 * (1 + kRopeConsumerWarps);
+constexpr int kRopeConsumerWarps = 8;        // default consumer warps per CTA
+constexpr int kRopeMaxConsumerWarps = 16;
+constexpr int kRopeRingMaxThreads = 32 * (1 + kRopeMaxConsumerWarps);
 constexpr int kRopeMaxTokensPerCta = 2048;
 
 __host__ __device__ inline uint32_t rope_stage_bytes(int Hq, int Hkv, int D, int rd, int elem_bytes, bool append) {
@@ -201,7 +202,7 @@ __host__ __device__ inline size_t rope_ring_smem_bytes(uint32_t stage, int stage
 }
 
 template <typename T, typename PosT, bool NEOX, bool APPEND>
-__global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeRingArgs a) {
+__global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const RopeRingArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int S = a.stages;
   const int NH = a.Hq + a.Hkv;
@@ -222,13 +223,13 @@ __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeR
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kRopeConsumerWarps);
+      mbar_init(&empty[s], (blockDim.x >> 5) - 1);  // one arrival per consumer warp
     }
     fence_barrier_init();
   }
   pdl_wait();
   const PosT* pos_p = static_cast<const PosT*>(a.pos) + tok0;
-  for (int i = tid; i < n; i += kRopeRingThreads) {
+  for (int i = tid; i < n; i += blockDim.x) {
     const int64_t pos = (int64_t)pos_p[i];
     const bool valid = pos >= 0 && pos < a.P;
     if (!valid) flag_status(a.status, MAS_STATUS_ROPE_POS_OUT_OF_RANGE);
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(kRopeRingThreads) rope_ring_kernel(const RopeR
     }
   } else {
     const int ct = tid - 32;
-    constexpr int ncons = 32 * kRopeConsumerWarps;
+    const int ncons = blockDim.x - 32;
     const int tpu = a.rd >> 4;  // threads' worth of 8-pair groups per head
     const int half = a.rd >> 1;
     const int groups = NH * tpu;
