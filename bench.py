@@ -62,6 +62,21 @@ def measured_peak() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each workload's dominant
+# kernel, from one ncu capture of that workload (summaries and commands in profiles/). Reads equal the
+# algorithmic bytes; writes come out lower because dirty lines still in the 126 MB L2 when the kernel
+# ends are not counted.
+NCU_TRAFFIC = {
+    "chain": (214_014_208 + 156_158_976, "profiles/norm_row_chain_shape.md"),
+    "norm_chain": (214_014_208 + 156_158_976, "profiles/norm_row_chain_shape.md"),
+    "norm": (83_929_344 + 25_862_656, "profiles/norm_loop_config1.md"),
+    "norm_fp8": (83_932_416 + 11_052_544, "profiles/ops_dram_traffic.md"),
+    "silu": (1_073_793_792 + 484_039_168, "profiles/ops_dram_traffic.md"),
+    "silu_fp8": (1_073_966_592 + 214_110_720, "profiles/ops_dram_traffic.md"),
+    "embed": (163_652_608 + 116_655_104, "profiles/ops_dram_traffic.md"),
+}
+
+
 # --------------------------------------------------------------------------------------------------
 # Process group.
 # --------------------------------------------------------------------------------------------------
@@ -314,6 +329,15 @@ class ChainWorkload:
         b.positions.copy_(self.host_pos, non_blocking=True)
         self._step(None)
         self.host_out.copy_(b.residual, non_blocking=True)
+
+    def digest(self) -> dict:
+        """This rank's output fingerprint (outside the timed region): its token count and the integer
+        sums of the final residual and hidden bit patterns. Rank 0 of an N-GPU run processes the
+        same step as a 1-GPU run, so with equal --steps/--warmup its digest equals the 1-GPU one."""
+        b = self.b
+        return {"tokens": int(self.tokens),
+                "residual_bits_sum": int(b.residual.view(torch.int16).to(torch.int64).sum().item()),
+                "hidden_bits_sum": int(b.hidden.view(torch.int16).to(torch.int64).sum().item())}
 
     def e2e_bytes(self) -> tuple[int, int]:
         return (self.host_ids.numel() * 8 + self.host_pos.numel() * 4,
@@ -646,6 +670,13 @@ def run_gpu_arm(args, dist: Dist) -> None:
                "sample": f"{tokens} of {w.tokens} tokens, all {layers} layers, C oracle, median of 3 steps "
                          f"({sum(times):.1f} s of CPU work)"}
 
+    # ---- outputs gathered for checking (NCCL, outside every timed region) ------------------------
+    gathered = None
+    if hasattr(w, "digest"):
+        per_rank = dist.gather_objects(w.digest())
+        gathered = {"ranks": dist.world, "per_rank": per_rank,
+                    "tokens_total": sum(d["tokens"] for d in per_rank)}
+
     if dist.rank != 0:
         return
     peak, peak_kind = measured_peak()
@@ -657,9 +688,12 @@ def run_gpu_arm(args, dist: Dist) -> None:
     roof = None
     if dom_ms is not None:
         achieved = w.dominant_bytes_per_launch() / (dom_ms / 1e3) / 1e9
+        traffic, traffic_src = args.traffic, "--traffic" if args.traffic is not None else None
+        if traffic is None and args.impl == "mas" and args.workload in NCU_TRAFFIC:
+            traffic, traffic_src = NCU_TRAFFIC[args.workload]
         roof = {"bound": "hbm", "kernel": w.dominant, "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                "traffic": args.traffic, "bytes_per_launch": w.dominant_bytes_per_launch(),
+                "traffic": traffic, "traffic_source": traffic_src, "bytes_per_launch": w.dominant_bytes_per_launch(),
                 "avg_launch_us": dom_ms * 1e3, "launches_timed": len(dom)}
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
@@ -671,6 +705,8 @@ def run_gpu_arm(args, dist: Dist) -> None:
         "gpu_launches": (w.launches_per_step() * args.steps) if args.impl == "mas" else 0,
         "clocks": clocks.summary(),
     }
+    if gathered is not None:
+        line["gathered_outputs"] = gathered
     if args.impl != "mas":
         line["impl"] = args.impl
     print(json.dumps(line))

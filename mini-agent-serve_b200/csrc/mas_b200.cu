@@ -355,8 +355,15 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
                        int enable_pdl) {
   const uint32_t stage = rope_stage_bytes(r.Hq, r.Hkv, r.D, r.rd, 2, APPEND);
   static const int env_stages = env_int("MAS_ROPE_STAGES", 0);
-  const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 4));
-  const size_t per_cta = rope_ring_smem_bytes(stage, stages, kRopeMaxTokensPerCta, APPEND);
+  static const int env_warps = env_int("MAS_ROPE_CONSUMER_WARPS", 0);
+  static const int env_ctas = env_int("MAS_ROPE_CTAS_PER_SM", 0);
+  const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 3));
+  const int threads = 32 * (1 + std::max(1, std::min(kRopeMaxConsumerWarps, env_warps > 0 ? env_warps : kRopeConsumerWarps)));
+  // The grid has at least one CTA per SM, so a CTA holds the positions of at most ceil(T / SMs)
+  // tokens; with that bound the shared memory per CTA is known before the CTA count is chosen.
+  // (rounded up to 64 tokens, which keeps the occupancy cache small across batch sizes).
+  const int tok_cap = (int)std::min<int64_t>(kRopeMaxTokensPerCta, ceil_div(ceil_div(r.T, (int64_t)st->sm_count), 64) * 64);
+  const size_t per_cta = rope_ring_smem_bytes(stage, stages, tok_cap, APPEND);
   if (per_cta > kMaxSmemPerCta) return kNotLaunched;
   const void* fn = bf ? (i64 ? (neox ? (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, true, APPEND>
                                      : (const void*)rope_ring_kernel<__nv_bfloat16, int64_t, false, APPEND>)
@@ -366,10 +373,10 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
                                      : (const void*)rope_ring_kernel<__half, int64_t, false, APPEND>)
                              : (neox ? (const void*)rope_ring_kernel<__half, int32_t, true, APPEND>
                                      : (const void*)rope_ring_kernel<__half, int32_t, false, APPEND>));
-  int ctas = (int)std::max<size_t>(1, kRingBytesPerSm / per_cta);
-  static const int env_warps = env_int("MAS_ROPE_CONSUMER_WARPS", 0);
-  const int threads = 32 * (1 + std::max(1, std::min(kRopeMaxConsumerWarps, env_warps > 0 ? env_warps : kRopeConsumerWarps)));
-  ctas = std::min(ctas, resident_ctas(fn, threads, per_cta));
+  // As many CTAs per SM as shared memory, registers and threads allow: the consumer side, not the
+  // depth of one ring, limits a CTA (measured at the chain shape: 2-3 CTAs of 3 stages beat one of 4-8).
+  int ctas = std::max(1, resident_ctas(fn, threads, per_cta));
+  if (env_ctas > 0) ctas = std::min(ctas, env_ctas);
   int64_t grid = std::max<int64_t>((int64_t)st->sm_count * ctas, ceil_div(r.T, kRopeMaxTokensPerCta));
   grid = std::min<int64_t>(grid, r.T);
   r.tokens_per_cta = (int32_t)ceil_div(r.T, grid);
