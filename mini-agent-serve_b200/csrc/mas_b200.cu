@@ -357,7 +357,9 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
   static const int env_stages = env_int("MAS_ROPE_STAGES", 0);
   static const int env_warps = env_int("MAS_ROPE_CONSUMER_WARPS", 0);
   static const int env_ctas = env_int("MAS_ROPE_CTAS_PER_SM", 0);
-  const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : 3));
+  // Two stages for small per-token stages (configuration 3: 10.75 KB), three for large ones (the chain
+  // shape: 27 KB); measured best of 2-4 stages x 8-16 consumer warps at both shapes.
+  const int stages = std::max(2, std::min(16, env_stages > 0 ? env_stages : (stage <= 16384 ? 2 : 3)));
   const int threads = 32 * (1 + std::max(1, std::min(kRopeMaxConsumerWarps, env_warps > 0 ? env_warps : kRopeConsumerWarps)));
   // The grid has at least one CTA per SM, so a CTA holds the positions of at most ceil(T / SMs)
   // tokens; with that bound the shared memory per CTA is known before the CTA count is chosen.
