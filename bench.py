@@ -272,10 +272,13 @@ class ChainWorkload:
     EVENT_EVERY = 16  # layers 8, 24, 40, 56, 72 carry events around both of their norms
     per_launch_value = False
 
-    def __init__(self, device, dist: Dist, ops, layers: int):
+    def __init__(self, device, dist: Dist, ops, layers: int, quant: bool = False):
         from mas_b200 import workloads as wl
         from mas_b200.chain import LayerChain
 
+        self.quant = quant
+        if quant:
+            self.name, self.dominant = "chain_fp8", "fused_add_rmsnorm_quant"
         self.wl = wl
         self.shape = wl.CHAIN_SHAPE
         ids, pos = wl.chain_host_inputs(replicas=dist.world)
@@ -285,8 +288,9 @@ class ChainWorkload:
         self.host_pos = pos[s:e].clone().pin_memory()
         self.tokens = per
         self.global_tokens = ids.shape[0]
-        self.b = wl.chain_buffers(self.host_ids, self.host_pos, device=device, seed=4 + dist.rank, layers=layers)
-        self.chain = LayerChain(self.shape, quant=False, layers=layers)
+        self.b = wl.chain_buffers(self.host_ids, self.host_pos, device=device, seed=4 + dist.rank, layers=layers,
+                                  quant=quant)
+        self.chain = LayerChain(self.shape, quant=quant, layers=layers)
         self.chain_ops = ops
         self.layers = self.chain.layers
         self.host_out = torch.empty(self.b.residual.shape, dtype=self.b.residual.dtype).pin_memory()
@@ -309,7 +313,11 @@ class ChainWorkload:
             if timed:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(st)
-            o.fused_add_rmsnorm(b.hidden, b.residual, b.w_in[l], eps, enable_pdl=True)
+            if self.quant:
+                o.fused_add_rmsnorm_quant(b.x_fp8, b.hidden, b.residual, b.w_in[l], b.act_scale[0:1], eps,
+                                          enable_pdl=True)
+            else:
+                o.fused_add_rmsnorm(b.hidden, b.residual, b.w_in[l], eps, enable_pdl=True)
             if timed:
                 e1.record(st)
                 dom_events.append((e0, e1))
@@ -317,11 +325,18 @@ class ChainWorkload:
             if timed:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(st)
-            o.fused_add_rmsnorm(b.attn_out, b.residual, b.w_post[l], eps, enable_pdl=True)
+            if self.quant:
+                o.fused_add_rmsnorm_quant(b.x_fp8, b.attn_out, b.residual, b.w_post[l], b.act_scale[1:2], eps,
+                                          enable_pdl=True)
+            else:
+                o.fused_add_rmsnorm(b.attn_out, b.residual, b.w_post[l], eps, enable_pdl=True)
             if timed:
                 e1.record(st)
                 dom_events.append((e0, e1))
-            o.silu_and_mul(b.gate_up, out=b.act, enable_pdl=True)
+            if self.quant:
+                o.silu_and_mul_quant(b.gate_up, b.act_scale[2:3], out=b.act_fp8, enable_pdl=True)
+            else:
+                o.silu_and_mul(b.gate_up, out=b.act, enable_pdl=True)
 
     def step(self, dom_events=None):
         self._step(dom_events)
@@ -353,10 +368,15 @@ class ChainWorkload:
         return self.chain.step_bytes(self.tokens)
 
     def dominant_bytes_per_launch(self) -> int:
-        return 8 * self.tokens * self.shape.hidden_size + 2 * self.shape.hidden_size
+        return (7 if self.quant else 8) * self.tokens * self.shape.hidden_size + 2 * self.shape.hidden_size
 
     def config(self) -> dict:
-        return chain_config(self.layers, self.tokens, self.global_tokens)
+        cfg = chain_config(self.layers, self.tokens, self.global_tokens)
+        if self.quant:
+            cfg["workload"] = ("chain, fp8 form (the decoder layers' own calls): embed + 88 x [RMSNorm+res -> e4m3, "
+                               "rope q/k, RMSNorm+res -> e4m3, SiLU-mul -> e4m3]")
+            cfg["norm"] = "fused_add_rmsnorm_quant"
+        return cfg
 
 
 class OpWorkload:
@@ -609,7 +629,10 @@ def run_gpu_arm(args, dist: Dist) -> None:
 
         mas_b200.prepare_device(device.index)
     layers = args.layers or 88
-    w = ChainWorkload(device, dist, ops, layers) if args.workload == "chain" else OpWorkload(args.workload, device, dist, ops)
+    if args.workload in ("chain", "chain_fp8"):
+        w = ChainWorkload(device, dist, ops, layers, quant=args.workload == "chain_fp8")
+    else:
+        w = OpWorkload(args.workload, device, dist, ops)
 
     st = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -640,7 +663,7 @@ def run_gpu_arm(args, dist: Dist) -> None:
 
     # ---- end-to-end through the public API with host inputs/outputs --------------------------------
     e2e = None
-    if args.workload == "chain" and not args.no_e2e:
+    if args.workload in ("chain", "chain_fp8") and not args.no_e2e:
         for _ in range(max(1, args.warmup // 2)):
             w.e2e_step()
         torch.cuda.synchronize()
@@ -722,7 +745,8 @@ def main(argv=None) -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["mas", "reference", "flashinfer"], default="mas")
     ap.add_argument("--workload", choices=["chain", "norm", "norm_fp8", "silu", "rope", "embed", "norm_chain",
-                                           "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain", "rope_append"],
+                                           "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain", "rope_append",
+                                           "chain_fp8"],
                     default="chain")
     ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
     ap.add_argument("--no-e2e", action="store_true")

@@ -2,7 +2,7 @@
 //
 // Bulk copies are the TMA engine's non-tensor form (cp.async.bulk): a contiguous run of bytes
 // between global and shared memory, completion tracked by an mbarrier transaction count (loads) or
-// a bulk async-group (stores). No multicast form is used anywhere in this library.
+// a bulk async-group (stores). Every copy has exactly one destination CTA: this GPU's own.
 #pragma once
 
 #include <cuda_runtime.h>
