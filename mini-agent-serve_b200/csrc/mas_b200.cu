@@ -238,12 +238,13 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
   static const bool use_ring = env_is("MAS_NORM_IMPL", "ring");
   static const bool use_row = env_is("MAS_NORM_IMPL", "row");
   static const bool use_loop = env_is("MAS_NORM_IMPL", "loop");
-  // Default: the persistent loop up to H = 6144 (config 1's H = 5120 measured 26.6 us against 29.5
+  // Default: the persistent loop up to H = 6144 (config 1's H = 5120 measured 26.3 us against 29.5
   // for the row-block grid), the row-block grid above (H = 12288: 67 us against 73+ for the loop).
   if (fast_ok && H % 8 == 0 && (use_loop || (!use_ring && !use_row && H <= 6144))) {
     // Persistent row-group loop (norm_loop_kernel): S-stage ring, every thread a consumer. By
-    // default at most 4 vectors per thread (threads per row = H/32, rounded up to a warp), two rows
-    // per CTA and two stages, which leaves two CTAs per SM at H = 5120.
+    // default at most 4 vectors per thread (threads per row = H/32, rounded up to a warp), CTAs of at
+    // least 128 threads (one row each from 128 threads per row up) and two stages: at H = 5120, four
+    // CTAs of one row per SM (e4m3 out: 25.8 us against 26.5 for two CTAs of two rows).
     static const int env_tpr = env_int("MAS_NORM_TPR", 0);
     static const int env_cta = env_int("MAS_NORM_CTA_THREADS", 0);
     static const int env_stages = env_int("MAS_NORM_STAGES", 0);
@@ -251,7 +252,7 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
     int tpr = (int)ceil_div(ceil_div(H / 8, 4), 32) * 32;
     if (env_tpr > 0) tpr = env_tpr;
     tpr = std::max(32, std::min(tpr, kNormRowMaxThreads)) / 32 * 32;
-    int cta = env_cta > 0 ? env_cta : std::min(2 * tpr, kNormRowMaxThreads);
+    int cta = env_cta > 0 ? env_cta : std::max(tpr, 128 / tpr * tpr);
     cta = std::max(tpr, std::min(cta, kNormRowMaxThreads)) / tpr * tpr;
     const int rpc = cta / tpr;
     const int vpt = (int)ceil_div(H / 8, tpr);
