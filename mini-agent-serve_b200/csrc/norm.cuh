@@ -6,16 +6,18 @@
 // and the norm is taken over the UNROUNDED h: y = h * rsqrt(sum(h^2)/H + eps) * w, rounded once.
 // The e4m3 variant multiplies by 1/scale, clamps to +-448 and rounds to nearest even.
 //
-// Fast path (rows of H % 8 == 0 elements, 16-byte aligned rows): a persistent, warp-specialised
-// TMA ring. Each CTA owns a contiguous block of rows. Warp 0 is the producer: one lane streams whole
-// rows of x and r into an S-stage shared-memory ring with two bulk copies per row (cp.async.bulk,
-// completion on the stage's `full` mbarrier), refilling a stage as soon as every consumer warp has
-// released it on the stage's `empty` mbarrier. The consumer warps form `groups` groups; group g takes
-// rows g, g + groups, ..., so that many rows are in their reduction phase at once. Within a group
-// each thread owns the same VPT 16-byte column slots of every row: it waits on `full`, forms
-// h = x + r in registers, stores round(h) to the residual, releases the stage, reduces sum(h^2)
-// through warp shuffles and one named barrier of its group, and stores the normalised row. The
-// weight slice lives in registers for the whole kernel. Every wait is bounded.
+// Fast paths (rows of H % 8 == 0 elements, 16-byte aligned rows), all staging whole rows of x and r
+// in shared memory with bulk copies (cp.async.bulk) and keeping the thread's weight slice in
+// registers:
+//   - norm_loop_kernel (the default up to H = 6144): a persistent grid; each CTA loops over row
+//     groups with the next group's copies in flight in a small ring, every thread a consumer;
+//   - norm_row_kernel (the default above): one short-lived CTA per group of rows, one mbarrier;
+//   - norm_tma_kernel (selectable, and the path for rows too wide for the others): a persistent,
+//     warp-specialised ring. Warp 0's first lane streams rows into an S-stage ring (`full`
+//     mbarriers); the consumer warps form `groups` groups, group g taking rows g, g + groups, ...,
+//     so that several rows are in their reduction phase at once, and release stages on `empty`
+//     mbarriers. S must be a multiple of `groups` (see the kernel).
+// Every wait is bounded.
 //
 // Generic path (any H, stride or alignment): one CTA per row, two passes over global memory; the
 // second pass recomputes h from the still-unmodified inputs, so no scratch space is needed.

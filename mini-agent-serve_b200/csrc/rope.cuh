@@ -5,7 +5,12 @@
 // cos = cache[pos, i], sin = cache[pos, rotary_dim/2 + i]; fp32 math, rounded once per element.
 // Neox pairs element i with i + rotary_dim/2; the interleaved form pairs 2i with 2i + 1.
 //
-// Work unit = one (token, head). A unit is handled by rotary_dim/16 threads; thread j of a unit
+// Three paths. The default, when q heads and k heads are each contiguous within a token (as for
+// q/k views of one fused qkv row), is the token-staged TMA ring further below (rope_ring_kernel),
+// which can also append k and v to the paged KV cache in the same pass. Padded heads take the vector
+// kernel described next, and odd rotary_dim or alignment the generic one.
+//
+// Vector kernel: work unit = one (token, head). A unit is handled by rotary_dim/16 threads; thread j of a unit
 // owns the 8 pairs whose cos/sin are cache[pos, 8j .. 8j+8), so each thread does exactly two
 // 16-byte loads and two 16-byte stores of q/k (both halves of its pairs) plus four 16-byte cos/sin
 // loads that hit L1 for all heads of a token after the first. Units run token-major, heads of one
