@@ -389,20 +389,21 @@ class OpWorkload:
         self.workload = name
         self.dev = device
         cs = wl.CHAIN_SHAPE
-        if name in ("norm", "norm_fp8", "norm_chain"):
-            if name == "norm_chain":
+        if name in ("norm", "norm_fp8", "norm_chain", "norm_fp8_chain"):
+            chain = name.endswith("_chain")
+            quant = name.startswith("norm_fp8")
+            if chain:
                 self.x, self.r, self.w, self.eps = wl.norm_inputs(device, seed=4, tokens=4352, hidden=cs.hidden_size)
             else:
                 self.x, self.r, self.w, self.eps = wl.norm_inputs(device)
             self.T, H = self.x.shape
             self.out = torch.empty(self.x.shape, dtype=torch.float8_e4m3fn, device=device)
             self.scale = torch.tensor([0.05], device=device)
-            self.bytes = (7 if name == "norm_fp8" else 8) * self.T * H + 2 * H
-            self.cfg = {"workload": f"{'chain-shape' if name == 'norm_chain' else 'config 1'} "
-                                    f"{'fp8-out ' if name == 'norm_fp8' else ''}RMSNorm+residual",
+            self.bytes = (7 if quant else 8) * self.T * H + 2 * H
+            self.cfg = {"workload": f"{'chain-shape' if chain else 'config 1'} "
+                                    f"{'fp8-out ' if quant else ''}RMSNorm+residual",
                         "tokens": self.T, "hidden": H, "l2": "inputs larger than L2"}
-            if name == "norm_chain":
-                self.name = "norm"
+            self.name = "norm_fp8" if quant else "norm"
         elif name in ("silu", "silu_chain", "silu_fp8", "silu_fp8_chain"):
             chain = name.endswith("_chain")
             quant = name.startswith("silu_fp8")
@@ -746,7 +747,7 @@ def main(argv=None) -> None:
     ap.add_argument("--impl", choices=["mas", "reference", "flashinfer"], default="mas")
     ap.add_argument("--workload", choices=["chain", "norm", "norm_fp8", "silu", "rope", "embed", "norm_chain",
                                            "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain", "rope_append",
-                                           "chain_fp8"],
+                                           "chain_fp8", "norm_fp8_chain"],
                     default="chain")
     ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
     ap.add_argument("--no-e2e", action="store_true")

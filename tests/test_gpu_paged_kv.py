@@ -248,3 +248,35 @@ def test_paged_empty_batches(cuda):
     mas_b200.apply_rope_and_append_paged_kv_cache(z32, q, q[:, : H * D], e, D, torch.zeros(8, D, device=cuda), z32,
                                                   (kc, kc.clone()), z32, indptr, last)
     assert int(kc.abs().sum()) == 0
+
+
+def test_append_and_fused_fp16(cuda):
+    """fp16 k/v/cache (the kv_cache_dtype override of model_config.py:57-66 keeps the model dtype)."""
+    Hq, H, D = 4, 2, 128
+    b, qkv, cache, kc, vc = _setup(51, Hq, H, D)
+    qkv, kc, vc = qkv.to(torch.float16), kc.to(torch.float16), vc.to(torch.float16)
+    T = qkv.shape[0]
+    bd = b.to(cuda)
+    qkv_d, kc_d, vc_d = qkv.to(cuda), kc.to(cuda), vc.to(cuda)
+    q_d, k_d, v_d = _split(qkv_d, Hq, H, D)
+    mas_b200.apply_rope_and_append_paged_kv_cache(bd.positions, q_d, k_d, v_d, D, cache.to(cuda), bd.batch_indices,
+                                                  (kc_d, vc_d), bd.kv_indices, bd.kv_indptr, bd.kv_last_page_len)
+    q, k, v = _split(qkv, Hq, H, D)
+    oracle.rope_append_paged_kv_cache(b.positions, q, k, v, D, cache, b.batch_indices, (kc, vc), b.kv_indices,
+                                      b.kv_indptr)
+    assert_ulp(qkv_d.cpu(), qkv, what="fp16 q/k")
+    assert_ulp(kc_d.cpu(), kc, what="fp16 k cache")
+    assert_bits_equal(vc_d, vc, "fp16 v cache")
+    # and the standalone append of the (now rotated) k rows
+    kc2, vc2 = torch.zeros_like(kc_d), torch.zeros_like(vc_d)
+    mas_b200.append_paged_kv_cache(k_d.view(T, H, D), v_d, bd.batch_indices, bd.positions, (kc2, vc2), bd.kv_indices,
+                                   bd.kv_indptr, bd.kv_last_page_len)
+    kw, vw = torch.zeros_like(kc), torch.zeros_like(vc)
+    oracle.append_paged_kv_cache(k_d.cpu().view(T, H, D), v_d.cpu(), b.batch_indices, b.positions, (kw, vw),
+                                 b.kv_indices, b.kv_indptr)
+    assert_bits_equal(kc2, kw, "fp16 append k")
+    assert_bits_equal(vc2, vw, "fp16 append v")
+
+
+def test_rope_append_hnd_partial_rotary_interleaved(cuda):
+    _fused(cuda, 52, 8, 2, 128, rd=64, hnd=True, neox=False, beta=0.05, orig=512)
