@@ -285,8 +285,6 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
     tpr = std::max(32, std::min(tpr, kNormRowMaxThreads)) / 32 * 32;
     cta = std::max(tpr, std::min(cta, kNormRowMaxThreads)) / tpr * tpr;
     const int rpc = cta / tpr;
-    static const int env_chunks = env_int("MAS_NORM_CHUNKS", 0);
-    a.chunks = env_chunks > 0 ? env_chunks : 1;
     const size_t smem = norm_row_smem_bytes(H, rpc, (int)sizeof(T));
     const int vpt = (int)ceil_div(H / 8, tpr);
     if (smem <= kMaxSmemPerCta && vpt <= 16) {

@@ -41,7 +41,6 @@ struct NormArgs {
   int32_t stages;       // ring depth (fast path)
   int32_t rows_per_cta; // fast path
   int32_t groups;       // fast path: consumer groups per CTA (rows k = g, g + groups, ... per group)
-  int32_t chunks;       // row-block path: bulk-copy chunks per row (pass 1 starts on the first)
   float eps;
   int32_t* fault;       // library fault word (bulk-copy timeouts)
 };
@@ -231,24 +230,19 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
 }
 
 // Row-block variant of the fast path: a non-persistent grid of small CTAs, each owning `rpc` rows
-// handled by `tpr` threads apiece. Thread 0 stages all of the CTA's x and r rows with bulk copies,
-// cut into up to kNormRowMaxChunks column chunks with one mbarrier each, so that the first pass
-// starts on the first chunk while the rest are still landing. Each row's threads then form h from
-// shared memory, reduce it (warp shuffles, a shared partial sum per warp, one CTA barrier) and write
-// both outputs, re-reading h from shared memory for the second pass. Several such CTAs per SM keep
-// several rows in their reduction phase at once. Every wait is bounded.
+// handled by `tpr` threads apiece. Thread 0 stages all of the CTA's x and r rows with bulk copies
+// on one mbarrier; each row's threads then form h from shared memory, reduce it (warp shuffles, a
+// shared partial sum per warp, one CTA barrier) and write both outputs, re-reading h from shared
+// memory for the second pass. Several such CTAs per SM keep several rows in their reduction phase
+// at once. The wait is bounded.
 constexpr int kNormRowMaxThreads = 512;
-constexpr int kNormRowMaxChunks = 4;
 
 __host__ __device__ inline size_t norm_row_smem_bytes(int H, int rpc, int elem_bytes) {
-  return (size_t)rpc * 2 * (size_t)H * (size_t)elem_bytes + kNormRowMaxChunks * 8 +
-         (size_t)(kNormRowMaxThreads / 32) * sizeof(float);
+  return (size_t)rpc * 2 * (size_t)H * (size_t)elem_bytes + 16 + (size_t)(kNormRowMaxThreads / 32) * sizeof(float);
 }
 
 // MAXV bounds the 16-byte vectors a thread handles per row (ceil(H/8 / tpr)); the thread's weight
 // slice is loaded into registers before the row arrives, so its latency overlaps the bulk copies.
-// Iteration j of a thread covers vectors [j*tpr, (j+1)*tpr) of the row, so chunk boundaries fall
-// between iterations: chunk c holds iterations [c*per, (c+1)*per).
 template <typename T, bool QUANT, int MAXV>
 __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const NormArgs a, int tpr, int rpc) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -256,19 +250,15 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
   const int NV = H >> 3;
   const uint32_t row_bytes = (uint32_t)H * (uint32_t)sizeof(T);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + (size_t)rpc * 2 * row_bytes);
-  float* red = reinterpret_cast<float*>(bar + kNormRowMaxChunks);
+  float* red = reinterpret_cast<float*>(bar + 2);
   const int tid = threadIdx.x;
   const int rr = tid / tpr;   // row slot of this thread within the CTA
   const int rt = tid - rr * tpr;
   const int64_t row0 = (int64_t)blockIdx.x * rpc;
   const int nrows = (int)min((int64_t)rpc, a.rows - row0);
-  const int iters = (NV + tpr - 1) / tpr;
-  int nch = max(1, min(min(a.chunks, kNormRowMaxChunks), iters));
-  const int per = (iters + nch - 1) / nch;  // iterations per chunk
-  nch = (iters + per - 1) / per;            // no empty chunk
 
   if (tid == 0) {
-    for (int c = 0; c < nch; ++c) mbar_init(&bar[c], 1);
+    mbar_init(bar, 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -276,16 +266,11 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
   T* const xb = static_cast<T*>(a.x);
   T* const rb = static_cast<T*>(a.r);
   if (tid == 0) {
-    for (int c = 0; c < nch; ++c) {
-      const int v0 = c * per * tpr;
-      const int v1 = min(NV, (c + 1) * per * tpr);
-      const uint32_t cb = (uint32_t)(v1 - v0) * 16u;  // chunk bytes per row and tensor
-      mbar_arrive_expect_tx(&bar[c], (uint32_t)nrows * 2 * cb);
-      for (int i = 0; i < nrows; ++i) {
-        unsigned char* st = smem + (size_t)i * 2 * row_bytes + (size_t)v0 * 16;
-        bulk_load(st, xb + (row0 + i) * a.x_stride + (size_t)v0 * 8, cb, &bar[c]);
-        bulk_load(st + row_bytes, rb + (row0 + i) * a.r_stride + (size_t)v0 * 8, cb, &bar[c]);
-      }
+    mbar_arrive_expect_tx(bar, (uint32_t)nrows * 2 * row_bytes);
+    for (int i = 0; i < nrows; ++i) {
+      unsigned char* st = smem + (size_t)i * 2 * row_bytes;
+      bulk_load(st, xb + (row0 + i) * a.x_stride, row_bytes, bar);
+      bulk_load(st + row_bytes, rb + (row0 + i) * a.r_stride, row_bytes, bar);
     }
   }
   float inv_scale = 1.0f;
@@ -296,20 +281,18 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
     const int v = rt + j * tpr;
     if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
   }
+  const bool ok = mbar_wait_bounded(bar, 0);
   const bool active = rr < nrows;
   const int64_t row = row0 + rr;
   const unsigned char* sx = smem + (size_t)rr * 2 * row_bytes;
   const unsigned char* sr = sx + row_bytes;
 
-  bool ok = true;
   float ss = 0.f;
-  if (active) {
+  if (ok && active) {
 #pragma unroll
     for (int j = 0; j < MAXV; ++j) {
       const int v = rt + j * tpr;
       if (v >= NV) break;
-      if (j % per == 0) ok = ok && mbar_wait_bounded(&bar[j / per], 0);
-      if (!ok) break;
       float xf[8], rf[8];
       unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), xf);
       unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
@@ -326,7 +309,7 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
   if (__syncthreads_or(!ok)) {
     if (tid == 0) {
       atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
-      for (int c = 0; c < nch; ++c) (void)mbar_wait_bounded(&bar[c], 0);  // copies still landing
+      (void)mbar_wait_bounded(bar, 0);  // the copies may still be landing in this CTA's shared memory
     }
     pdl_launch_dependents();
     return;
