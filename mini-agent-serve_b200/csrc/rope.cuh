@@ -191,6 +191,7 @@ struct RopeRingArgs {
   const void* v;     // APPEND: v rows (heads contiguous), token stride vsn
   int64_t vsn;
   PagedKVArgs kv;
+  int32_t early_dependents;  // signal programmatic dependents after the prologue instead of at the end
 };
 
 constexpr int kRopeConsumerWarps = 8;        // default consumer warps per CTA
@@ -249,6 +250,10 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
     }
   }
   __syncthreads();
+  // The grid is resident (at most the SMs' capacity), so letting the next kernel's CTAs launch now
+  // only lets them take the SM space this kernel leaves free; their griddepcontrol.wait still waits
+  // for this whole grid to finish.
+  if (a.early_dependents) pdl_launch_dependents();
 
   T* const qb = static_cast<T*>(a.q);
   T* const kb = static_cast<T*>(a.k);
