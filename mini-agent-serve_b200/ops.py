@@ -252,6 +252,24 @@ def silu_and_mul_quant(input: torch.Tensor, scale: Union[float, torch.Tensor], o
 # ------------------------------------------------------------------------------------------------
 # Rotary embedding from the fp32 cos|sin cache.
 # ------------------------------------------------------------------------------------------------
+def _check_rope(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor, head_size: int,
+                cos_sin_cache: torch.Tensor) -> None:
+    """flashinfer's checks (FI/rope.py:1260-1261) plus the layout the kernels assume."""
+    if cos_sin_cache.dtype != torch.float32:
+        raise ValueError("cos_sin_cache should be float32")
+    if cos_sin_cache.dim() != 2 or not cos_sin_cache.is_contiguous():
+        raise ValueError("cos_sin_cache must be a contiguous (max_seq_len, rotary_dim) tensor")
+    if positions.dtype not in _ID_DTYPES:
+        raise ValueError(f"positions must be int32 or int64, got {positions.dtype}")
+    if query.dtype != key.dtype:
+        raise ValueError("query and key must share one dtype")
+    rotary_dim = cos_sin_cache.shape[1]
+    if rotary_dim % 2 != 0 or rotary_dim > head_size:
+        raise ValueError(f"rotary_dim {rotary_dim} must be even and <= head_size {head_size}")
+    if query.shape[0] != positions.shape[0] or key.shape[0] != positions.shape[0]:
+        raise ValueError("positions, query and key must have the same number of tokens")
+
+
 @torch.library.register_fake("mas_b200::apply_rope_pos_ids_cos_sin_cache")
 def _(q, k, cos_sin_cache, pos_ids, interleave, enable_pdl, status) -> None:
     return None
@@ -269,19 +287,7 @@ def apply_rope_with_cos_sin_cache_inplace(positions: torch.Tensor, query: torch.
     half-rotation (True) or the interleaved pairs (False). A ValueError is raised for a non-fp32
     cache. `enable_pdl` (an addition; the kernels are PDL-safe) defaults to True.
     """
-    if cos_sin_cache.dtype != torch.float32:
-        raise ValueError("cos_sin_cache should be float32")
-    if cos_sin_cache.dim() != 2 or not cos_sin_cache.is_contiguous():
-        raise ValueError("cos_sin_cache must be a contiguous (max_seq_len, rotary_dim) tensor")
-    if positions.dtype not in _ID_DTYPES:
-        raise ValueError(f"positions must be int32 or int64, got {positions.dtype}")
-    if query.dtype != key.dtype:
-        raise ValueError("query and key must share one dtype")
-    rotary_dim = cos_sin_cache.shape[1]
-    if rotary_dim % 2 != 0 or rotary_dim > head_size:
-        raise ValueError(f"rotary_dim {rotary_dim} must be even and <= head_size {head_size}")
-    if query.shape[0] != positions.shape[0] or key.shape[0] != positions.shape[0]:
-        raise ValueError("positions, query and key must have the same number of tokens")
+    _check_rope(positions, query, key, head_size, cos_sin_cache)
     if positions.shape[0] == 0:
         return
     q = query.view(query.shape[0], -1, head_size)
@@ -312,19 +318,7 @@ def apply_rope_and_llama4_query_scale_inplace(positions: torch.Tensor, query: to
     """
     if original_max_position_embeddings <= 0:
         raise ValueError("original_max_position_embeddings must be positive")
-    if cos_sin_cache.dtype != torch.float32:
-        raise ValueError("cos_sin_cache should be float32")
-    if cos_sin_cache.dim() != 2 or not cos_sin_cache.is_contiguous():
-        raise ValueError("cos_sin_cache must be a contiguous (max_seq_len, rotary_dim) tensor")
-    if positions.dtype not in _ID_DTYPES:
-        raise ValueError(f"positions must be int32 or int64, got {positions.dtype}")
-    if query.dtype != key.dtype:
-        raise ValueError("query and key must share one dtype")
-    rotary_dim = cos_sin_cache.shape[1]
-    if rotary_dim % 2 != 0 or rotary_dim > head_size:
-        raise ValueError(f"rotary_dim {rotary_dim} must be even and <= head_size {head_size}")
-    if query.shape[0] != positions.shape[0] or key.shape[0] != positions.shape[0]:
-        raise ValueError("positions, query and key must have the same number of tokens")
+    _check_rope(positions, query, key, head_size, cos_sin_cache)
     if positions.shape[0] == 0:
         return
     q = query.view(query.shape[0], -1, head_size)
@@ -445,20 +439,12 @@ def apply_rope_and_append_paged_kv_cache(positions: torch.Tensor, query: torch.T
     ``(nnz, heads, head_size)`` views; `value` ``(nnz, num_kv_heads, head_size)`` or flat.
     """
     k_cache, v_cache = _unpack_paged_kv_cache(paged_kv_cache, kv_layout)
-    if cos_sin_cache.dtype != torch.float32:
-        raise ValueError("cos_sin_cache should be float32")
-    if cos_sin_cache.dim() != 2 or not cos_sin_cache.is_contiguous():
-        raise ValueError("cos_sin_cache must be a contiguous (max_seq_len, rotary_dim) tensor")
-    if positions.dtype not in _ID_DTYPES:
-        raise ValueError(f"positions must be int32 or int64, got {positions.dtype}")
-    if not (query.dtype == key.dtype == value.dtype):
+    _check_rope(positions, query, key, head_size, cos_sin_cache)
+    if value.dtype != query.dtype:
         raise ValueError("query, key and value must share one dtype")
     _act_code(query)
-    rotary_dim = cos_sin_cache.shape[1]
-    if rotary_dim % 2 != 0 or rotary_dim > head_size:
-        raise ValueError(f"rotary_dim {rotary_dim} must be even and <= head_size {head_size}")
     nnz = positions.shape[0]
-    if query.shape[0] != nnz or key.shape[0] != nnz or value.shape[0] != nnz or batch_indices.shape != (nnz,):
+    if value.shape[0] != nnz or batch_indices.shape != (nnz,):
         raise ValueError("positions, batch_indices, query, key and value must have the same number of tokens")
     if llama_4_scaling_beta and original_max_position_embeddings <= 0:
         raise ValueError("original_max_position_embeddings must be positive")
