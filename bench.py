@@ -1,34 +1,43 @@
 """Benchmark of the B200 per-token layer ops (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mas|reference|flashinfer]
-                    [--workload chain|norm|norm_fp8|silu|rope|embed]
+                    [--workload chain|chain_fp8|norm|norm_fp8|silu|silu_fp8|rope|rope_append|embed|
+                                norm_chain|norm_fp8_chain|silu_chain|silu_fp8_chain|rope_chain]
 
 Default workload: configuration 5, the per-layer op chain at 123B-class shapes (H 12288, 96/8 heads,
 D 128, I 28672, V 131072): one step = embed + 88 x (input RMSNorm+residual, rope on q/k, post-attn
 RMSNorm+residual, SiLU-mul on [T, 57344]) over T = 256 decode + 2 x 2048 prefill tokens, with seeded
-random bf16 activations standing in for the attention and GEMM outputs (mas_b200.chain).
+random bf16 activations standing in for the attention and GEMM outputs (mas_b200.chain). `chain_fp8`
+is the same step with the calls the decoder layers actually make (e4m3-out norms, and SiLU-mul with
+the down projection's activation quantisation). The other workloads time one op per launch:
+configurations 1-4, their fp8 and paged-append forms, and the chain's shapes.
 
 Metric: tokens/s of the whole job (all ranks), plus the chain's algorithmic HBM GB/s and its fraction
 of the measured HBM peak. Multi-GPU (torchrun, one rank per GPU) is weak scaling: the global batch is
 N mixed steps and rank r takes the r-th, a contiguous slice; no collective touches the data path.
-NCCL only carries the barrier and the max-over-ranks of the timings (parity of the chain is checked
-by tests/test_gpu_chain.py against the oracle, outside the benchmark).
+NCCL only carries the barrier, the max-over-ranks of the timings and, after the timed regions, the
+gather of each rank's output digest (parity of the chain itself is checked by
+tests/test_gpu_chain.py against the oracle).
 
 Reported alongside the device-resident `value`:
   e2e            the same step through the public API with the step's host inputs (token ids,
-                 positions) copied from pinned memory and the result (the residual stream) read
-                 back, inside the timed region;
+                 positions) copied from pinned memory and the result (the residual stream) copied
+                 back to pinned memory on a second stream, overlapping the next step, all inside the
+                 timed region;
   roofline       the dominant kernel's algorithmic bytes / its CUDA-event time, against the measured
                  HBM copy peak (MEASURED_PEAKS.json); in the timed region, events bracket its
-                 launches in every 16th layer (both norms), so they barely perturb the step;
+                 launches in every 16th layer (both norms), so they barely perturb the step; `traffic`
+                 is that kernel's DRAM bytes from an ncu capture (NCU_TRAFFIC, profiles/);
   cpu_baseline   the C oracle (tests' checker, a restatement of the reference's arithmetic) timed
                  on this host's cores on a token sample of the same workload (rank 0, N = 1);
-  clocks         SM clock and throttle reasons sampled by nvidia-smi during the timed region.
+  clocks         SM clock and throttle reasons sampled by nvidia-smi during the timed region;
+  gathered_outputs  each rank's token count and output digest.
 
 --impl reference times the reference's CPU path: the reference has no CPU implementation of norm,
 silu or rope (its kernels are flashinfer's, CUDA-only), so this arm runs the C oracle port with all
 host threads on a token sample (embedding included), rank 0 only. --impl flashinfer times the
-reference's actual GPU kernels (flashinfer 0.6.11.post2, aten gather) on the same workload.
+reference's actual GPU kernels (flashinfer 0.6.11.post2, aten gather, the compiled quantize_fp8)
+on the same workload.
 """
 from __future__ import annotations
 
