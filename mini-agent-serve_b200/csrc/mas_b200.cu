@@ -571,9 +571,12 @@ static int silu_impl(void* out, const void* input, const float* scale, int64_t n
   const bool bf16 = dtype == MAS_DTYPE_BF16;
   if (vec && (quant || !use_ring)) {
     static const int env_rows = env_int("MAS_SILU_GRID_ROWS", 0);
-    // 16 row groups per SM: each thread walks a few rows, so CTA start-up is amortised without a tail
-    const int64_t rows = env_rows > 0 ? env_rows : 16 * (int64_t)st->sm_count;
-    const dim3 grid((unsigned)ceil_div(d / 8, kSiluThreads), (unsigned)std::min<int64_t>({num_tokens, rows, 65535}));
+    // About 16 row groups per SM: each thread walks a few rows, so CTA start-up is amortised. The
+    // group count is then evened out so that every group walks the same number of rows (at the
+    // chain shape, 4352 rows: 2176 groups of 2 rather than 2368 groups of 1 or 2).
+    const int64_t target = std::min<int64_t>({num_tokens, env_rows > 0 ? env_rows : 16 * (int64_t)st->sm_count, 65535});
+    const int64_t per = ceil_div(num_tokens, target);
+    const dim3 grid((unsigned)ceil_div(d / 8, kSiluThreads), (unsigned)ceil_div(num_tokens, per));
     const dim3 block(kSiluThreads);
     if (quant) {
       return bf16 ? launch(silu_mul_vec_kernel<__nv_bfloat16, true>, grid, block, 0, stream, enable_pdl, a)
