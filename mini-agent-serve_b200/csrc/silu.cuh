@@ -172,7 +172,14 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
   pdl_wait();
   const int nvec = a.d >> 3;
   const int v = blockIdx.x * kSiluThreads + threadIdx.x;
-  const QuantDiv div = make_quant_div(QUANT ? *a.scale : 1.0f);
+  QuantDiv div = {1.0f, 1.0f, true};
+  if constexpr (QUANT) {
+    // one reciprocal per CTA (the IEEE reciprocal is a multi-instruction sequence)
+    __shared__ QuantDiv sdiv;
+    if (threadIdx.x == 0) sdiv = make_quant_div(*a.scale);
+    __syncthreads();
+    div = sdiv;
+  }
   if (v < nvec) {
     for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
       const T* g = static_cast<const T*>(a.in) + row * a.in_stride + (size_t)v * 8;
