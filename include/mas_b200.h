@@ -72,6 +72,16 @@ MAS_API int mas_prepare_device(int device);
 MAS_API int mas_read_fault_word(int device, int32_t* value, int clear);
 
 /*
+ * Self-test of failure detection (no counterpart in the reference): launches one thread that waits
+ * on an mbarrier nothing completes, bounded by limit_ns nanoseconds (0 < limit_ns <= 2 s, the limit
+ * every kernel's own waits use), then sets MAS_STATUS_COPY_TIMEOUT in the library fault word, as a
+ * kernel whose bulk copy never landed does. The device stays usable; read the word with
+ * mas_read_fault_word. Used by the tests to show that a wait that runs out ends in a status the
+ * host can read, without faulting or hanging the GPU.
+ */
+MAS_API int mas_selftest_bounded_wait(int64_t limit_ns, void* stream);
+
+/*
  * Fused residual add + RMSNorm, in place, bf16/fp16:
  *   h = f32(input) + f32(residual);  residual <- round(h);
  *   input <- round(h * rsqrt(mean(h^2) + eps) * weight)      (mean over hidden_size, h unrounded)

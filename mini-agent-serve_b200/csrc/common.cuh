@@ -176,12 +176,13 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 // Waits for the phase with the given parity to complete; false if the time limit ran out first.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t polls = 1; polls < kWaitMaxPolls; ++polls) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((polls & 255u) == 0u && global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if ((polls & 255u) == 0u && global_timer_ns() - t0 > limit_ns) return false;
   }
   return false;
 }

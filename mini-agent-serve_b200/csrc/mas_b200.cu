@@ -462,6 +462,17 @@ int make_append_args(AppendArgs* out, const MasPagedKVCache* c, const int32_t* b
   return MAS_OK;
 }
 
+// Self-test of the bounded wait every bulk-copy consumer uses: one thread waits on an mbarrier that
+// nothing will ever complete, with the caller's time limit, then reports the timeout exactly as the
+// kernels do (MAS_STATUS_COPY_TIMEOUT in the fault word) and returns. No copy is in flight, so the
+// CTA can leave with the barrier pending.
+__global__ void selftest_wait_kernel(uint64_t limit_ns, int32_t* fault) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  if (!mbar_wait_bounded(&bar, 0, limit_ns)) atomicOr(fault, MAS_STATUS_COPY_TIMEOUT);
+}
+
 }  // namespace
 }  // namespace mas
 
@@ -500,6 +511,14 @@ int mas_read_fault_word(int device, int32_t* value, int clear) {
   }
   if (prev >= 0 && prev != device) (void)cudaSetDevice(prev);
   return e == cudaSuccess ? MAS_OK : (int)e;
+}
+
+int mas_selftest_bounded_wait(int64_t limit_ns, void* stream) {
+  if (limit_ns <= 0 || limit_ns > (int64_t)kWaitLimitNs) return MAS_ERR_INVALID_ARGUMENT;
+  DeviceState* st = nullptr;
+  int rc = current_device(&st);
+  if (rc != MAS_OK) return rc;
+  return launch(selftest_wait_kernel, dim3(1), dim3(1), 0, stream, 0, (uint64_t)limit_ns, st->fault);
 }
 
 int mas_fused_add_rmsnorm(void* input, void* residual, const void* weight, int64_t num_tokens,

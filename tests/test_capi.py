@@ -97,6 +97,8 @@ def _kv(page_size=16):
     (lambda: L.mas_fused_add_rmsnorm(P, P, P, 2, 8, 8, 8, 1e-5, 9, 0, None), -2),
     (lambda: L.mas_fused_add_rmsnorm_quant(P, P, P, P, P, 2, 8, 8, 8, 8, 1e-5, 0, 0, 0, None), -2),
     (lambda: L.mas_fused_add_rmsnorm_quant(P, P, P, P, None, 2, 8, 8, 8, 8, 1e-5, 0, 3, 0, None), -1),
+    (lambda: L.mas_selftest_bounded_wait(0, None), -1),
+    (lambda: L.mas_selftest_bounded_wait(3_000_000_000, None), -1),
     (lambda: L.mas_silu_and_mul(P, P, 2, 8, 8, 15, 0, 0, None), -1),
     (lambda: L.mas_silu_and_mul(P, P, 2, 8, 7, 16, 0, 0, None), -1),
     (lambda: L.mas_silu_and_mul(P, P, 2, 8, 8, 16, 2, 0, None), -2),
