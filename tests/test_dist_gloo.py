@@ -17,7 +17,6 @@ import socket
 import sys
 from pathlib import Path
 
-import pytest
 import torch
 import torch.multiprocessing as mp
 
