@@ -298,23 +298,6 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
         const int64_t t = tok0 + i;
         const int64_t slot = APPEND ? sslot[i] : -1;
         const float qs = a.q_beta != 0.f ? llama4_q_scale<T>(spos[i], a.q_beta, a.q_inv_orig) : 0.f;
-        // A thread's 8-pair group j within a head is the same for all its heads when the consumer
-        // count is a multiple of the groups per head (always, for rotary_dim/16 a power of two up
-        // to 16): its cos/sin then come from shared memory once per token, not once per head.
-        float cs[8], sn[8];
-        const auto load_cs = [&](int j) {
-          const float4 c0 = *reinterpret_cast<const float4*>(c + j * 8);
-          const float4 c1 = *reinterpret_cast<const float4*>(c + j * 8 + 4);
-          const float4 s0 = *reinterpret_cast<const float4*>(c + half + j * 8);
-          const float4 s1 = *reinterpret_cast<const float4*>(c + half + j * 8 + 4);
-          cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
-          cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-          sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
-          sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-        };
-        // (Not with APPEND: there the 16 extra live registers would cost a resident CTA per SM.)
-        const bool fixed_j = !APPEND && ncons % tpu == 0;
-        if (fixed_j && ct < groups) load_cs(ct % tpu);
         for (int gi = ct; gi < groups; gi += ncons) {
           const int h = gi / tpu;
           const int j = gi - h * tpu;
@@ -322,8 +305,17 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
           T* gh = h < a.Hq ? qb + t * a.qsn + (int64_t)h * a.D : kb + t * a.ksn + (int64_t)(h - a.Hq) * a.D;
           const int off0 = NEOX ? j * 8 : j * 16;
           const int off1 = NEOX ? half + j * 8 : j * 16 + 8;
-          float x0[8], x1[8], o0[8], o1[8];
-          if (!fixed_j) load_cs(j);
+          float cs[8], sn[8], x0[8], x1[8], o0[8], o1[8];
+          {
+            const float4 c0 = *reinterpret_cast<const float4*>(c + j * 8);
+            const float4 c1 = *reinterpret_cast<const float4*>(c + j * 8 + 4);
+            const float4 s0 = *reinterpret_cast<const float4*>(c + half + j * 8);
+            const float4 s1 = *reinterpret_cast<const float4*>(c + half + j * 8 + 4);
+            cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+            cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+            sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+            sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+          }
           unpack8<T>(*reinterpret_cast<const Vec16*>(sh + off0), x0);
           unpack8<T>(*reinterpret_cast<const Vec16*>(sh + off1), x1);
           if constexpr (NEOX) {
