@@ -16,7 +16,8 @@
  * Compiled with -ffp-contract=off so no multiply-add is fused behind the C source's back.
  *
  * Every entry point mirrors the argument order of the matching C-ABI function in
- * include/mas_b200.h (prefix orc_ instead of mas_), minus the stream and PDL flag.
+ * include/mas_b200.h (prefix orc_ instead of mas_), minus the stream and PDL flag; the paged-cache
+ * functions take the fields of MasPagedKVCache as separate arguments.
  */
 #include <math.h>
 #include <stdint.h>
