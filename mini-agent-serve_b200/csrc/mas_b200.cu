@@ -590,11 +590,11 @@ static int silu_impl(void* out, const void* input, const float* scale, int64_t n
   const bool bf16 = dtype == MAS_DTYPE_BF16;
   if (vec && (quant || !use_ring)) {
     static const int env_rows = env_int("MAS_SILU_GRID_ROWS", 0);
-    // About 16 row groups per SM: each thread walks a few rows, so CTA start-up is amortised. The
-    // e4m3 form is issue-bound and gains from longer-lived threads: 4 per SM, each walking four times
-    // the rows (chain shape: 109 us against 119 at 16 per SM). The group count is then evened out so
+    // About 20 row groups per SM: each thread walks a few rows, so CTA start-up is amortised (16-28
+    // per SM measured within 1 %). The e4m3 form is issue-bound and gains from longer-lived threads:
+    // 4 per SM (chain shape: 109 us against 119 at 16 per SM). The group count is then evened out so
     // that every group walks the same number of rows (4352 rows: 2176 groups of 2, not 2368 of 1-2).
-    const int64_t groups = env_rows > 0 ? env_rows : (quant ? 4 : 16) * (int64_t)st->sm_count;
+    const int64_t groups = env_rows > 0 ? env_rows : (quant ? 4 : 20) * (int64_t)st->sm_count;
     const int64_t target = std::min<int64_t>({num_tokens, groups, 65535});
     const int64_t per = ceil_div(num_tokens, target);
     const dim3 grid((unsigned)ceil_div(d / 8, kSiluThreads), (unsigned)ceil_div(num_tokens, per));
