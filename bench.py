@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mas|reference|flashinfer]
                     [--workload chain|chain_fp8|norm|norm_fp8|silu|silu_fp8|rope|rope_append|embed|
-                                norm_chain|norm_fp8_chain|silu_chain|silu_fp8_chain|rope_chain]
+                                embed_fill|norm_chain|norm_fp8_chain|silu_chain|silu_fp8_chain|rope_chain]
 
 Default workload: configuration 5, the per-layer op chain at 123B-class shapes (H 12288, 96/8 heads,
 D 128, I 28672, V 131072): one step = embed + 88 x (input RMSNorm+residual, rope on q/k, post-attn
@@ -240,6 +240,15 @@ class FlashinferOps:
         apply_rope_with_cos_sin_cache_inplace(positions, q, k, head_size, cache, is_neox=True)
         append_paged_kv_cache(k.view(T, -1, head_size), v.view(T, -1, head_size), batch_indices, positions,
                               paged_kv_cache, kv_indices, kv_indptr, kv_last_page_len, kv_layout="NHD")
+
+    @staticmethod
+    def embedding_fill_placeholders(ids, table, last):
+        """The reference's pair: ModelRunner.fill_placeholders (model_runner.py:149-154) then the
+        embedding gather."""
+        is_placeholder = ids < 0
+        rows = (-1 - ids).clamp(min=0)
+        ids.copy_(torch.where(is_placeholder, last[rows], ids))
+        return torch.index_select(table, 0, ids)
 
     _quantize = None
 
@@ -488,6 +497,24 @@ class OpWorkload:
             self.bytes = self.T * (2 * 2 * Hq * D + 3 * 2 * Hkv * D + 2 * 2 * Hkv * D + 4 * D + 12)
             self.cfg = {"workload": "config 3 rope q[T,32,128] k[T,8,128] + paged KV append (NHD, 16-token pages)",
                         "tokens": self.T, "pages": self.pb.num_pages, "l2": "inputs larger than L2"}
+        elif name == "embed_fill":
+            # A configuration-5 step's ids (int64, as the runner keeps them): the 256 decode rows hold
+            # placeholders -1 - r for the previous step's samples (model_runner.py:149-154).
+            ids, _ = wl.chain_host_inputs()
+            ids[:256] = -1 - torch.arange(256)
+            self.ids_init = ids.to(device)
+            self.ids = self.ids_init.clone()
+            self.last = torch.randint(0, cs.vocab_size, (256,), generator=torch.Generator().manual_seed(8),
+                                      dtype=torch.int64).to(device)
+            self.table = wl._normal((cs.vocab_size, cs.hidden_size), wl._gen(device, 3), device, torch.bfloat16,
+                                    std=0.02)
+            self.T = self.ids.shape[0]
+            self.out = torch.empty(self.T, self.table.shape[1], dtype=self.table.dtype, device=device)
+            # gather rows in and out, ids read and written back, the placeholders' samples
+            self.bytes = 2 * 2 * self.T * self.table.shape[1] + 2 * 8 * self.T + 8 * 256
+            self.cfg = {"workload": "chain-shape embedding gather with the runner's placeholder substitution (f4)",
+                        "tokens": self.T, "hidden": self.table.shape[1], "placeholders": 256,
+                        "l2": "table 3.2 GB > L2; output 107 MB"}
         elif name == "embed":
             self.table, self.ids = wl.embed_inputs(device)
             self.T = self.ids.shape[0]
@@ -510,6 +537,8 @@ class OpWorkload:
         # flush itself lands inside the timed launch). Each launch then reads its inputs from HBM.
         self.flush.zero_()
         self.flush_sum = self.flush.sum(dtype=torch.int32)
+        if self.name == "embed_fill":
+            self.ids.copy_(self.ids_init)  # the placeholders again (the op resolves them in place)
         if dom_events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
@@ -531,6 +560,8 @@ class OpWorkload:
                                                    pb.kv_indptr, pb.kv_last_page_len)
         elif n == "embed":
             o.embedding_out(self.out, self.ids, self.table)
+        elif n == "embed_fill":
+            self.out = o.embedding_fill_placeholders(self.ids, self.table, self.last)
         if dom_events is not None:
             e1.record(st)
             dom_events.append((e0, e1))
@@ -790,7 +821,7 @@ def main(argv=None) -> None:
     ap.add_argument("--impl", choices=["mas", "reference", "flashinfer"], default="mas")
     ap.add_argument("--workload", choices=["chain", "norm", "norm_fp8", "silu", "rope", "embed", "norm_chain",
                                            "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain", "rope_append",
-                                           "chain_fp8", "norm_fp8_chain"],
+                                           "chain_fp8", "norm_fp8_chain", "embed_fill"],
                     default="chain")
     ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
     ap.add_argument("--no-e2e", action="store_true")
