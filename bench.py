@@ -2,7 +2,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mas|reference|flashinfer]
                     [--workload chain|chain_fp8|norm|norm_fp8|silu|silu_fp8|rope|rope_append|embed|
-                                embed_fill|norm_chain|norm_fp8_chain|silu_chain|silu_fp8_chain|rope_chain]
+                                embed_fill|norm_chain|norm_fp8_chain|silu_chain|silu_fp8_chain|rope_chain|
+                                rope_qscale_chain]
 
 Default workload: configuration 5, the per-layer op chain at 123B-class shapes (H 12288, 96/8 heads,
 D 128, I 28672, V 131072): one step = embed + 88 x (input RMSNorm+residual, rope on q/k, post-attn
@@ -241,6 +242,14 @@ class FlashinferOps:
         append_paged_kv_cache(k.view(T, -1, head_size), v.view(T, -1, head_size), batch_indices, positions,
                               paged_kv_cache, kv_indices, kv_indptr, kv_last_page_len, kv_layout="NHD")
 
+    def apply_rope_and_llama4_query_scale_inplace(self, positions, q, k, head_size, cache, beta, orig, is_neox=True):
+        """The reference's sequence: flashinfer rope, then the eager llama-4 query scale into a new
+        tensor (devstral2.py:163-166, :175-179)."""
+        self.apply_rope_with_cos_sin_cache_inplace(positions, q, k, head_size, cache, is_neox=is_neox)
+        attn_scale = 1 + beta * torch.log1p(torch.floor(positions.float() / orig))
+        q3 = q.unflatten(-1, (-1, head_size))
+        return q3 * attn_scale[:, None, None].to(q.dtype)
+
     @staticmethod
     def embedding_fill_placeholders(ids, table, last):
         """The reference's pair: ModelRunner.fill_placeholders (model_runner.py:149-154) then the
@@ -467,7 +476,7 @@ class OpWorkload:
                                     f"{' + fp8 activation quant' if quant else ''}",
                         "tokens": self.T, "d": self.out.shape[1], "l2": "inputs larger than L2"}
             self.name = "silu_fp8" if quant else "silu"
-        elif name == "rope_chain":
+        elif name in ("rope_chain", "rope_qscale_chain"):
             ids, pos = wl.chain_host_inputs()
             b = wl.chain_buffers(ids, pos, device=device, layers=1)
             self.pos, self.cache = b.positions, b.cos_sin_cache
@@ -478,6 +487,11 @@ class OpWorkload:
             self.cfg = {"workload": "chain-shape rope: q/k strided views of qkv [4352, 14336], 96+8 heads",
                         "tokens": self.T, "l2": "inputs larger than L2"}
             self.name = "rope"
+            if name == "rope_qscale_chain":
+                # Devstral2Attention's llama-4 query scale (devstral2.py:175-179) fused into rope (f1)
+                self.beta, self.orig = 0.1, 8192
+                self.cfg["workload"] = "chain-shape rope + llama-4 query scale (beta 0.1, original max 8192)"
+                self.name = "rope_qscale"
         elif name == "rope":
             self.pos, self.q, self.k, self.cache = wl.rope_inputs(device)
             self.T = self.pos.shape[0]
@@ -553,6 +567,9 @@ class OpWorkload:
             o.silu_and_mul_quant(self.x, self.scale, out=self.out, enable_pdl=True)
         elif n == "rope":
             o.apply_rope_with_cos_sin_cache_inplace(self.pos, self.q, self.k, 128, self.cache, is_neox=True)
+        elif n == "rope_qscale":
+            self.q_scaled = o.apply_rope_and_llama4_query_scale_inplace(
+                self.pos, self.q, self.k, 128, self.cache, self.beta, self.orig, is_neox=True)
         elif n == "rope_append":
             pb = self.pb
             o.apply_rope_and_append_paged_kv_cache(pb.positions, self.q, self.k, self.v, 128, self.cache,
@@ -821,7 +838,7 @@ def main(argv=None) -> None:
     ap.add_argument("--impl", choices=["mas", "reference", "flashinfer"], default="mas")
     ap.add_argument("--workload", choices=["chain", "norm", "norm_fp8", "silu", "rope", "embed", "norm_chain",
                                            "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain", "rope_append",
-                                           "chain_fp8", "norm_fp8_chain", "embed_fill"],
+                                           "chain_fp8", "norm_fp8_chain", "embed_fill", "rope_qscale_chain"],
                     default="chain")
     ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
     ap.add_argument("--no-e2e", action="store_true")
