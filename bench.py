@@ -86,6 +86,7 @@ NCU_TRAFFIC = {
     "rope": (328_030_464 + 254_389_504, "profiles/ops_dram_traffic.md"),
     "rope_chain": (118_126_336 + 59_780_608, "profiles/rope_ring_chain_shape.md"),
     "silu_fp8_chain": (499_139_840 + 69_091_072, "profiles/ops_dram_traffic.md"),
+    "rope_append_small": (383_577_088 + 381_649_152, "profiles/rope_append_config3_small.md"),
 }
 
 
@@ -498,8 +499,11 @@ class OpWorkload:
             self.bytes = self.T * (2 * 2 * (self.q.shape[1] + self.k.shape[1]) + 4 * 128 + 4)
             self.cfg = {"workload": "config 3 rope q[T,32,128] k[T,8,128]", "tokens": self.T,
                         "l2": "inputs larger than L2 (689 MB)"}
-        elif name == "rope_append":
-            self.pb, self.qkv, self.cache, self.kc, self.vc = wl.rope_append_inputs(device)
+        elif name in ("rope_append", "rope_append_small"):
+            # _small: the same tokens with cached prefixes below 4096 positions, so the page pool (and the
+            # device memory an ncu capture saves and restores) is about 20 times smaller
+            self.pb, self.qkv, self.cache, self.kc, self.vc = wl.rope_append_inputs(
+                device, max_offset=4096 if name == "rope_append_small" else 65536)
             Hq, Hkv, D = 32, 8, 128
             self.q = self.qkv[:, : Hq * D]
             self.k = self.qkv[:, Hq * D: (Hq + Hkv) * D]
@@ -509,8 +513,10 @@ class OpWorkload:
             # q read+write, k read + write back + cache write, v read + cache write, cos|sin row,
             # position, batch index, page-table entry
             self.bytes = self.T * (2 * 2 * Hq * D + 3 * 2 * Hkv * D + 2 * 2 * Hkv * D + 4 * D + 12)
-            self.cfg = {"workload": "config 3 rope q[T,32,128] k[T,8,128] + paged KV append (NHD, 16-token pages)",
+            self.cfg = {"workload": "config 3 rope q[T,32,128] k[T,8,128] + paged KV append (NHD, 16-token pages)"
+                        + (", cached prefixes < 4096" if name == "rope_append_small" else ""),
                         "tokens": self.T, "pages": self.pb.num_pages, "l2": "inputs larger than L2"}
+            self.name = self.dominant = "rope_append"
         elif name == "embed_fill":
             # A configuration-5 step's ids (int64, as the runner keeps them): the 256 decode rows hold
             # placeholders -1 - r for the previous step's samples (model_runner.py:149-154).
@@ -838,7 +844,8 @@ def main(argv=None) -> None:
     ap.add_argument("--impl", choices=["mas", "reference", "flashinfer"], default="mas")
     ap.add_argument("--workload", choices=["chain", "norm", "norm_fp8", "silu", "rope", "embed", "norm_chain",
                                            "silu_chain", "rope_chain", "silu_fp8", "silu_fp8_chain", "rope_append",
-                                           "chain_fp8", "norm_fp8_chain", "embed_fill", "rope_qscale_chain"],
+                                           "chain_fp8", "norm_fp8_chain", "embed_fill", "rope_qscale_chain",
+                                           "rope_append_small"],
                     default="chain")
     ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
     ap.add_argument("--no-e2e", action="store_true")

@@ -151,11 +151,11 @@ def paged_batch_from_lengths(cached, new, page_size: int = 16, spare_pages: int 
 
 def rope_append_inputs(device="cuda", seed: int = 2, num_q_heads: int = 32, num_kv_heads: int = 8,
                        head_dim: int = 128, page_size: int = 16, max_positions: int = 131072, theta: float = 1e9,
-                       dtype=torch.bfloat16):
+                       dtype=torch.bfloat16, max_offset: int = 65536):
     """Configuration 3's ragged batch (64 sequences of U[1, 1024] new tokens after random cached
-    prefixes) as one prefill step over a paged cache: (PagedBatch on device, qkv [T, (Hq+2Hkv)*D],
-    cos|sin cache, k_cache, v_cache [pages, page_size, Hkv, D])."""
-    rb = rope_batch(seed)
+    prefixes below `max_offset`) as one prefill step over a paged cache: (PagedBatch on device,
+    qkv [T, (Hq+2Hkv)*D], cos|sin cache, k_cache, v_cache [pages, page_size, Hkv, D])."""
+    rb = rope_batch(seed, max_offset=max_offset)
     starts = torch.cumsum(rb.seq_lens, 0) - rb.seq_lens
     cached = rb.positions[starts.long()].tolist()
     b = paged_batch_from_lengths(cached, rb.seq_lens.tolist(), page_size, 5, torch.Generator().manual_seed(seed))
