@@ -8,9 +8,14 @@ flashinfer 0.6.11.post2 functions that miniagentserve/models/devstral2/devstral2
     fused_add_rmsnorm_quant    FI/norm/__init__.py:288-344         devstral2.py:241-252
     silu_and_mul               FI/activation.py:77-118             devstral2.py:223-224
     apply_rope_with_cos_sin_cache_inplace  FI/rope.py:1223-1272    devstral2.py:163-166
+    append_paged_kv_cache      FI/page.py:280-406                  devstral2.py:170-173
 
 plus the token-embedding gather behind nn.Embedding (devstral2.py:260, :282), as `embedding` and the
-`Embedding` module (embedding.py).
+`Embedding` module (embedding.py). Four fused forms, each one launch where the reference makes
+several, are additions: silu_and_mul_quant (SiLU-mul then FP8Linear's quantisation),
+apply_rope_and_llama4_query_scale_inplace, apply_rope_and_append_paged_kv_cache (rope, the paged
+append and optionally the query scale) and embedding_fill_placeholders (the runner's placeholder
+substitution then the gather).
 
 Each function is a thin Python check layer (raising flashinfer's exception types) over a
 `mas_b200::*` torch operator. The operators are defined and implemented in C++
