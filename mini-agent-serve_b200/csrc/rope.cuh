@@ -78,6 +78,32 @@ __device__ __forceinline__ float scaled_q(float rotated, float scale) {
   return __fmul_rn(Elem<T>::to_f(Elem<T>::from_f(rotated)), scale);
 }
 
+// The same scale applied to eight rotated q values already packed as T, two per packed multiply.
+// The product of two bf16 (8-bit significands) or two fp16 (11-bit) values is exact in fp32, so the
+// packed multiply's single rounding to T equals scaled_q's fp32 product rounded to T.
+template <typename T>
+__device__ __forceinline__ uint32_t mul2_rn(uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ uint32_t mul2_rn<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  const __nv_bfloat162 r = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                                      *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+template <>
+__device__ __forceinline__ uint32_t mul2_rn<__half>(uint32_t a, uint32_t b) {
+  const __half2 r = __hmul2_rn(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+template <typename T>
+__device__ __forceinline__ Vec16 scaled_q8(const Vec16& v, uint32_t scale2) {
+  Vec16 r;
+  r.a = mul2_rn<T>(v.a, scale2);
+  r.b = mul2_rn<T>(v.b, scale2);
+  r.c = mul2_rn<T>(v.c, scale2);
+  r.d = mul2_rn<T>(v.d, scale2);
+  return r;
+}
+
 // Each thread group handles kRopeUnits adjacent units per iteration (usually heads of one token,
 // so the position and the cos/sin row are shared). All q/k loads of the iteration are issued before
 // the position is checked: a load never waits on another load's latency, and a position out of
@@ -298,6 +324,7 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
         const int64_t t = tok0 + i;
         const int64_t slot = APPEND ? sslot[i] : -1;
         const float qs = a.q_beta != 0.f ? llama4_q_scale<T>(spos[i], a.q_beta, a.q_inv_orig) : 0.f;
+        const uint32_t qs2 = Elem<T>::from_f2(qs, qs);  // exact: qs is already a T value
         for (int gi = ct; gi < groups; gi += ncons) {
           const int h = gi / tpu;
           const int j = gi - h * tpu;
@@ -328,16 +355,14 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
               rotate(x1[2 * e], x1[2 * e + 1], cs[4 + e], sn[4 + e], o1[2 * e], o1[2 * e + 1]);
             }
           }
-          if (a.q_beta != 0.f && h < a.Hq) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              o0[e] = scaled_q<T>(o0[e], qs);
-              o1[e] = scaled_q<T>(o1[e], qs);
-            }
-          }
           const Vec16 p0 = pack8<T>(o0), p1 = pack8<T>(o1);
-          st_plain(gh + off0, p0);
-          st_plain(gh + off1, p1);
+          if (a.q_beta != 0.f && h < a.Hq) {
+            st_plain(gh + off0, scaled_q8<T>(p0, qs2));
+            st_plain(gh + off1, scaled_q8<T>(p1, qs2));
+          } else {
+            st_plain(gh + off0, p0);
+            st_plain(gh + off1, p1);
+          }
           if (APPEND && h >= a.Hq && slot >= 0) {
             T* ch = static_cast<T*>(a.kv.k_cache) + slot + (int64_t)(h - a.Hq) * a.kv.stride_head;
             st_plain(ch + off0, p0);
