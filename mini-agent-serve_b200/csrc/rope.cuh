@@ -312,6 +312,10 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
     const int tpu = a.rd >> 4;  // threads' worth of 8-pair groups per head
     const int half = a.rd >> 1;
     const int groups = NH * tpu;
+    // When the consumer count is a multiple of tpu, every thread keeps one pair group j for all heads
+    // and tokens: its cos/sin values are read once per token and the heads follow by a fixed step.
+    const bool fixed_j = ncons % tpu == 0;
+    const int jf = ct % tpu, h0 = ct / tpu, hstep = ncons / tpu;
     for (int i = 0; i < n; ++i) {
       const int s = i % S;
       if (!mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u)) {
@@ -325,24 +329,13 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
         const int64_t slot = APPEND ? sslot[i] : -1;
         const float qs = a.q_beta != 0.f ? llama4_q_scale<T>(spos[i], a.q_beta, a.q_inv_orig) : 0.f;
         const uint32_t qs2 = Elem<T>::from_f2(qs, qs);  // exact: qs is already a T value
-        for (int gi = ct; gi < groups; gi += ncons) {
-          const int h = gi / tpu;
-          const int j = gi - h * tpu;
+        // One group: the 8 rotation pairs of staged head h held in the 16-byte vectors at off0, off1.
+        const auto group = [&](int h, int j, const float (&cs)[8], const float (&sn)[8]) {
           const T* sh = reinterpret_cast<const T*>(st) + (size_t)h * a.D;  // staged head (q then k)
           T* gh = h < a.Hq ? qb + t * a.qsn + (int64_t)h * a.D : kb + t * a.ksn + (int64_t)(h - a.Hq) * a.D;
           const int off0 = NEOX ? j * 8 : j * 16;
           const int off1 = NEOX ? half + j * 8 : j * 16 + 8;
-          float cs[8], sn[8], x0[8], x1[8], o0[8], o1[8];
-          {
-            const float4 c0 = *reinterpret_cast<const float4*>(c + j * 8);
-            const float4 c1 = *reinterpret_cast<const float4*>(c + j * 8 + 4);
-            const float4 s0 = *reinterpret_cast<const float4*>(c + half + j * 8);
-            const float4 s1 = *reinterpret_cast<const float4*>(c + half + j * 8 + 4);
-            cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
-            cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-            sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
-            sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-          }
+          float x0[8], x1[8], o0[8], o1[8];
           unpack8<T>(*reinterpret_cast<const Vec16*>(sh + off0), x0);
           unpack8<T>(*reinterpret_cast<const Vec16*>(sh + off1), x1);
           if constexpr (NEOX) {
@@ -367,6 +360,30 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
             T* ch = static_cast<T*>(a.kv.k_cache) + slot + (int64_t)(h - a.Hq) * a.kv.stride_head;
             st_plain(ch + off0, p0);
             st_plain(ch + off1, p1);
+          }
+        };
+        // cos/sin of pair group j (cos in c[0, half), sin in c[half, rd)).
+        const auto load_cs = [&](int j, float (&cs)[8], float (&sn)[8]) {
+          const float4 c0 = *reinterpret_cast<const float4*>(c + j * 8);
+          const float4 c1 = *reinterpret_cast<const float4*>(c + j * 8 + 4);
+          const float4 s0 = *reinterpret_cast<const float4*>(c + half + j * 8);
+          const float4 s1 = *reinterpret_cast<const float4*>(c + half + j * 8 + 4);
+          cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
+          cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+          sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+          sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+        };
+        if (fixed_j) {
+          float cs[8], sn[8];
+          load_cs(jf, cs, sn);
+          for (int h = h0; h < NH; h += hstep) group(h, jf, cs, sn);
+        } else {
+          for (int gi = ct; gi < groups; gi += ncons) {
+            const int h = gi / tpu;
+            const int j = gi - h * tpu;
+            float cs[8], sn[8];
+            load_cs(j, cs, sn);
+            group(h, j, cs, sn);
           }
         }
         if constexpr (APPEND) {
