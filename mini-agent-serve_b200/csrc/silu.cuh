@@ -136,6 +136,7 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
 // not a normal number; the IEEE divide is used then.
 struct QuantDiv {
   float scale, r;
+  float r_lo, r_hi;  // RN(r * (1 -+ 2^-20)): brackets for quant2_e4m3
   bool fast;
   __device__ __forceinline__ float operator()(float x) const {
     if (!fast) return __fdiv_rn(x, scale);
@@ -150,6 +151,8 @@ __device__ __forceinline__ QuantDiv make_quant_div(float s) {
   QuantDiv d;
   d.scale = s;
   d.r = __frcp_rn(s);
+  d.r_lo = __fmul_rn(d.r, 1.0f - 0x1p-20f);
+  d.r_hi = __fmul_rn(d.r, 1.0f + 0x1p-20f);
   d.fast = fabsf(s) >= 0x1p-126f && fabsf(s) <= 0x1.fffffep127f && fabsf(d.r) >= 0x1p-126f &&
            fabsf(d.r) <= 0x1.fffffep127f;
   return d;
@@ -158,9 +161,24 @@ __device__ __forceinline__ QuantDiv make_quant_div(float s) {
 // FP8Linear's activation quantisation of four silu outputs (already rounded to the activation type):
 // (act / scale) in fp32, clamped to +-448 and rounded to nearest even e4m3 (satfinite does the
 // clamp; NaN stays NaN, as with a clamp that propagates it).
+//
+// Two activations at a time, usually without forming the quotient: x * r_lo and x * r_hi bracket
+// RN_f32(x / scale) (each carries at most three roundings of 2^-24 against the 2^-20 margin), and
+// rounding to e4m3 is monotonic, so when both brackets round to the same code that code is the
+// quotient's. Otherwise (a bracket straddles an e4m3 rounding boundary: about 1e-5 of inputs for a
+// general scale, up to 0.3 % for a power-of-two scale, whose quotients can land on exact ties) the
+// pair takes the remainder-corrected quotient. Checked on the CPU over every bf16 and fp16 input.
+__device__ __forceinline__ uint16_t quant2_e4m3(float x0, float x1, const QuantDiv& div) {
+  if (div.fast) {
+    const uint16_t lo = f2_to_e4m3x2(__fmul_rn(x0, div.r_lo), __fmul_rn(x1, div.r_lo));
+    const uint16_t hi = f2_to_e4m3x2(__fmul_rn(x0, div.r_hi), __fmul_rn(x1, div.r_hi));
+    if (lo == hi) return lo;
+  }
+  return f2_to_e4m3x2(div(x0), div(x1));
+}
+
 __device__ __forceinline__ uint32_t quant4_e4m3(const float* act, const QuantDiv& div) {
-  return (uint32_t)f2_to_e4m3x2(div(act[0]), div(act[1])) |
-         ((uint32_t)f2_to_e4m3x2(div(act[2]), div(act[3])) << 16);
+  return (uint32_t)quant2_e4m3(act[0], act[1], div) | ((uint32_t)quant2_e4m3(act[2], act[3], div) << 16);
 }
 
 // Register variant (the default fast path): one 16-byte gate/up pair per thread and row, 32
@@ -172,7 +190,7 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
   pdl_wait();
   const int nvec = a.d >> 3;
   const int v = blockIdx.x * kSiluThreads + threadIdx.x;
-  QuantDiv div = {1.0f, 1.0f, true};
+  QuantDiv div = {1.0f, 1.0f, 1.0f, 1.0f, true};
   if constexpr (QUANT) {
     // one reciprocal per CTA (the IEEE reciprocal is a multi-instruction sequence)
     __shared__ QuantDiv sdiv;

@@ -45,9 +45,10 @@ def test_silu_quant_shapes(cuda, T, d):
     _check(cuda, T, d, 0.0137)
 
 
-@pytest.mark.parametrize("scale", [1e-3, 0.05, 1.7, 300.0])
+@pytest.mark.parametrize("scale", [1e-3, 0.05, 1.7, 300.0, 0.125, 4.0])
 def test_silu_quant_scales_and_saturation(cuda, scale):
-    """A small scale drives most outputs to +-448 (saturation); a large one into e4m3 subnormals."""
+    """A small scale drives most outputs to +-448 (saturation); a large one into e4m3 subnormals.
+    Power-of-two scales put many quotients exactly on e4m3 ties (the kernel's exact fallback)."""
     _check(cuda, 6, 2048, scale)
 
 
