@@ -85,8 +85,8 @@ NCU_TRAFFIC = {
     "silu_fp8": (1_073_966_592 + 214_110_720, "profiles/ops_dram_traffic.md"),
     "embed": (163_652_608 + 116_655_104, "profiles/ops_dram_traffic.md"),
     "rope": (328_030_464 + 254_389_504, "profiles/ops_dram_traffic.md"),
-    "rope_chain": (118_126_336 + 59_780_608, "profiles/rope_ring_chain_shape.md"),
-    "silu_fp8_chain": (499_139_840 + 69_091_072, "profiles/ops_dram_traffic.md"),
+    "rope_chain": (118_129_152 + 59_046_912, "profiles/rope_ring_chain_shape.md"),
+    "silu_fp8_chain": (499_136_256 + 73_464_832, "profiles/silu_fp8_chain_shape.md"),
     "rope_append_small": (383_577_088 + 381_649_152, "profiles/rope_append_config3_small.md"),
 }
 
