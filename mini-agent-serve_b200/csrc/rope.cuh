@@ -395,7 +395,9 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
             const int n_copy = n_tail + a.Hkv * d_v;
             const T* sk = reinterpret_cast<const T*>(st + q_bytes);
             const T* sv = reinterpret_cast<const T*>(st + q_bytes + k_bytes);
-            for (int u = ct; u < n_copy; u += ncons) {
+            // Copies go to the highest-numbered consumers first: with fixed pair groups the lowest-
+            // numbered ones take the extra heads, so this evens out the work per thread and token.
+            for (int u = ncons - 1 - ct; u < n_copy; u += ncons) {
               if (u < n_tail) {
                 const int h = u / tail_v, j = u - h * tail_v;
                 const int off = a.rd + j * 8;
