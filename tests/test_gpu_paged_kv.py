@@ -150,7 +150,7 @@ def test_rope_append_llama4_scale(cuda):
     _fused(cuda, 33, 8, 2, 128, beta=0.1, orig=64)
 
 
-@pytest.mark.parametrize("rd", [64, 32])
+@pytest.mark.parametrize("rd", [64, 32, 96])  # 96: consumers walk the (head, pair group) list
 def test_rope_append_partial_rotary_with_scale(cuda, rd):
     """The k tail past rotary_dim goes to the cache unrotated; q's tail is scaled by the tail launch."""
     _fused(cuda, 34, 4, 2, 128, rd=rd, beta=0.2, orig=128)

@@ -59,7 +59,9 @@ def test_rope_int64_positions(cuda):
     _run(cuda, 23, 4, 2, 128, 128, 4096, pos_dtype=torch.int64)
 
 
-@pytest.mark.parametrize("D,rd", [(128, 64), (128, 32), (40, 40), (128, 72)])
+# rotary_dim 48, 96, 112: rotary_dim/16 does not divide the ring's consumer count, so its consumers
+# walk the (head, pair group) list instead of keeping one pair group each
+@pytest.mark.parametrize("D,rd", [(128, 64), (128, 32), (40, 40), (128, 72), (128, 48), (128, 96), (128, 112)])
 def test_rope_partial_and_generic_rotary(cuda, D, rd):
     _run(cuda, 11, 3, 1, D, rd, 64)
 
