@@ -56,6 +56,15 @@ _ACT_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_FP16}
 _ID_DTYPES = {torch.int32: _lib.DTYPE_INT32, torch.int64: _lib.DTYPE_INT64}
 
 
+def _check_device(ref: torch.Tensor, **tensors: Optional[torch.Tensor]) -> None:
+    """Every tensor argument on `ref`'s device, as aten and flashinfer require: a kernel handed a host
+    tensor would be given a host pointer. Raises RuntimeError, as torch does for the same mistake."""
+    for name, t in tensors.items():
+        if t is not None and t.device != ref.device:
+            raise RuntimeError(f"Expected all tensors to be on the same device, but {name} is on {t.device} "
+                               f"and the other operands on {ref.device}")
+
+
 def _act_code(t: torch.Tensor) -> int:
     try:
         return _ACT_DTYPES[t.dtype]
@@ -146,6 +155,7 @@ def fused_add_rmsnorm(input: torch.Tensor, residual: torch.Tensor, weight: torch
     Same signature and meaning as flashinfer.norm.fused_add_rmsnorm (FI/norm/__init__.py:236-274).
     """
     _check_norm(input, residual, weight)
+    _check_device(input, residual=residual, weight=weight)
     _OP_NORM(input, residual, weight, float(eps), True if enable_pdl is None else bool(enable_pdl))
 
 
@@ -185,6 +195,7 @@ def fused_add_rmsnorm_quant(out: torch.Tensor, input: torch.Tensor, residual: to
         raise ValueError(f"out must be {FP8}, got {out.dtype}")
     if out.shape != input.shape:
         raise ValueError(f"out {tuple(out.shape)} and input {tuple(input.shape)} differ")
+    _check_device(input, out=out, residual=residual, weight=weight)
     scale = _normalize_scale(scale, input)
     _OP_NORM_QUANT(out, input, residual, weight, scale, float(eps), True if enable_pdl is None else bool(enable_pdl))
 
@@ -218,6 +229,7 @@ def silu_and_mul(input: torch.Tensor, out: Optional[torch.Tensor] = None,
         _check_shape(input, out)
         if out.dtype != input.dtype:
             raise ValueError("out must have the dtype of input")
+        _check_device(input, out=out)
     else:
         out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), device=input.device, dtype=input.dtype)
     _act_code(input)
@@ -246,6 +258,7 @@ def silu_and_mul_quant(input: torch.Tensor, scale: Union[float, torch.Tensor], o
         _check_shape(input, out)
         if out.dtype != FP8:
             raise ValueError(f"out must be {FP8}, got {out.dtype}")
+        _check_device(input, out=out)
     else:
         out = torch.empty(input.shape[:-1] + (input.shape[-1] // 2,), device=input.device, dtype=FP8)
     _act_code(input)
@@ -273,6 +286,7 @@ def _check_rope(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
         raise ValueError(f"rotary_dim {rotary_dim} must be even and <= head_size {head_size}")
     if query.shape[0] != positions.shape[0] or key.shape[0] != positions.shape[0]:
         raise ValueError("positions, query and key must have the same number of tokens")
+    _check_device(query, positions=positions, key=key, cos_sin_cache=cos_sin_cache)
 
 
 @torch.library.register_fake("mas_b200::apply_rope_pos_ids_cos_sin_cache")
@@ -413,6 +427,8 @@ def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor, 
     if positions.dtype not in _ID_DTYPES:
         positions = positions.int()
     _check_paged(k_cache, v_cache, kv_indptr, kv_last_page_len, heads, head_size, kv_layout, append_key.dtype)
+    _check_device(append_key, append_value=append_value, batch_indices=batch_indices, positions=positions,
+                  k_cache=k_cache, v_cache=v_cache, kv_indices=kv_indices, kv_indptr=kv_indptr)
     if nnz == 0:
         return
     _OP_APPEND(append_key, append_value, _int32(batch_indices), positions.contiguous(), k_cache, v_cache,
@@ -457,6 +473,8 @@ def apply_rope_and_append_paged_kv_cache(positions: torch.Tensor, query: torch.T
     if v.shape != k.shape:
         raise ValueError("key and value must have the same heads")
     _check_paged(k_cache, v_cache, kv_indptr, kv_last_page_len, k.shape[1], head_size, kv_layout, query.dtype)
+    _check_device(query, value=value, batch_indices=batch_indices, k_cache=k_cache, v_cache=v_cache,
+                  kv_indices=kv_indices, kv_indptr=kv_indptr)
     if nnz == 0:
         return
     _OP_ROPE_APPEND(q, k, v, cos_sin_cache, positions.contiguous(), _int32(batch_indices), k_cache, v_cache,
@@ -483,6 +501,7 @@ def _check_embedding(input_ids: torch.Tensor, weight: torch.Tensor) -> None:
         raise ValueError(f"input_ids must be int32 or int64, got {input_ids.dtype}")
     if weight.dim() != 2 or weight.stride(1) != 1:
         raise ValueError("weight must be a (num_embeddings, embedding_dim) tensor, contiguous in its last dimension")
+    _check_device(weight, input_ids=input_ids)
 
 
 def embedding(input_ids: torch.Tensor, weight: torch.Tensor, enable_pdl: Optional[bool] = None) -> torch.Tensor:
@@ -503,6 +522,7 @@ def embedding_out(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tens
         raise ValueError("out must be (*input_ids.shape, embedding_dim) with weight's dtype")
     if not out.is_contiguous():
         raise ValueError("out must be contiguous")
+    _check_device(weight, out=out)
     _OP_EMBED_OUT(out, input_ids.contiguous(), weight, True if enable_pdl is None else bool(enable_pdl),
                   _status_arg(weight.device))
     return out
@@ -530,6 +550,7 @@ def embedding_fill_placeholders(input_ids: torch.Tensor, weight: torch.Tensor, l
     _check_embedding(input_ids, weight)
     if last_tokens.dtype not in _ID_DTYPES:
         raise ValueError(f"last_tokens must be int32 or int64, got {last_tokens.dtype}")
+    _check_device(weight, last_tokens=last_tokens)
     if not input_ids.is_contiguous():
         raise ValueError("input_ids must be contiguous (it is updated in place)")
     return _OP_EMBED_FILL(input_ids, weight, last_tokens.contiguous(),

@@ -174,3 +174,50 @@ def test_seeded_host_inputs():
     b = wl.rope_batch()
     assert b.seq_lens.shape == (64,) and int(b.seq_lens.min()) >= 1 and int(b.seq_lens.max()) <= 1024
     assert b.positions.shape[0] == int(b.seq_lens.sum()) and int(b.positions.max()) < 65536 + 1024
+
+
+def test_operands_on_another_device_are_rejected_before_any_launch():
+    """A host tensor among device operands raises (as aten does) instead of reaching a kernel as a
+    host pointer. Meta tensors stand in for the device here; the mismatch is caught in Python."""
+    C = torch.device("cpu")
+    x = torch.empty(4, 64, dtype=BF, device=M)
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.fused_add_rmsnorm(x, torch.empty(4, 64, dtype=BF, device=M), torch.empty(64, dtype=BF, device=C))
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.fused_add_rmsnorm_quant(torch.empty(4, 64, dtype=torch.float8_e4m3fn, device=C), x,
+                                         torch.empty(4, 64, dtype=BF, device=M), torch.empty(64, dtype=BF, device=M),
+                                         torch.ones(1, device=M))
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.silu_and_mul(torch.empty(4, 64, dtype=BF, device=M), out=torch.empty(4, 32, dtype=BF, device=C))
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.silu_and_mul_quant(torch.empty(4, 64, dtype=BF, device=M), torch.ones(1, device=M),
+                                    out=torch.empty(4, 32, dtype=torch.float8_e4m3fn, device=C))
+    q, k = torch.empty(3, 2 * 128, dtype=BF, device=M), torch.empty(3, 128, dtype=BF, device=M)
+    pos = torch.zeros(3, dtype=torch.int32, device=M)
+    cache = torch.empty(16, 128, device=M)
+    for bad in ({"positions": torch.zeros(3, dtype=torch.int32)}, {"cos_sin_cache": torch.empty(16, 128)}):
+        args = {"positions": pos, "cos_sin_cache": cache} | bad
+        with pytest.raises(RuntimeError, match="same device"):
+            mas_b200.apply_rope_with_cos_sin_cache_inplace(args["positions"], q, k, 128, args["cos_sin_cache"])
+        with pytest.raises(RuntimeError, match="same device"):
+            mas_b200.apply_rope_and_llama4_query_scale_inplace(args["positions"], q, k, 128, args["cos_sin_cache"],
+                                                               0.1, 8192)
+    kc = torch.empty(4, 16, 1, 128, dtype=BF, device=M)
+    ind = torch.zeros(4, dtype=torch.int32, device=M)
+    indptr = torch.tensor([0, 4], dtype=torch.int32, device=M)
+    last = torch.ones(1, dtype=torch.int32, device=M)
+    bi = torch.zeros(3, dtype=torch.int32, device=M)
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.append_paged_kv_cache(k.view(3, 1, 128), k.view(3, 1, 128), bi, pos, (kc, kc), torch.zeros(4, dtype=torch.int32), indptr, last)
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.apply_rope_and_append_paged_kv_cache(pos, q, k, k.clone(), 128, cache, torch.zeros(3, dtype=torch.int32),
+                                                      (kc, kc), ind,
+                                                      indptr, last)
+    table = torch.empty(10, 64, dtype=BF, device=M)
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.embedding_gather(torch.zeros(3, dtype=torch.int64), table)
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.embedding_out(torch.empty(3, 64, dtype=BF), torch.zeros(3, dtype=torch.int64, device=M), table)
+    with pytest.raises(RuntimeError, match="same device"):
+        mas_b200.embedding_fill_placeholders(torch.zeros(3, dtype=torch.int64, device=M), table,
+                                             torch.zeros(2, dtype=torch.int64))
