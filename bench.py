@@ -14,31 +14,35 @@ the down projection's activation quantisation). The other workloads time one op 
 configurations 1-4, their fp8 and paged-append forms, and the chain's shapes.
 
 Metric: tokens/s of the whole job (all ranks), plus the chain's algorithmic HBM GB/s and its fraction
-of the measured HBM peak. Multi-GPU (torchrun, one rank per GPU) is weak scaling: the global batch is
-N mixed steps and rank r takes the r-th, a contiguous slice; no collective touches the data path.
-NCCL only carries the barrier, the max-over-ranks of the timings and, after the timed regions, the
-gather of each rank's output digest (parity of the chain itself is checked by
-tests/test_gpu_chain.py against the oracle).
+of the measured HBM peak. Multi-GPU (torchrun, one rank per GPU): the headline is weak scaling (the
+global batch is N mixed steps and rank r takes the r-th, a contiguous slice); no collective touches
+the data path. NCCL only carries barriers, the max over ranks of the timings and, after the timed
+regions, the gather of every rank's sampled outputs for the oracle check.
 
-Reported alongside the device-resident `value`:
-  e2e            the same step through the public API with the step's host inputs (token ids,
-                 positions) copied from pinned memory and the result (the residual stream) copied
-                 back to pinned memory on a second stream, overlapping the next step, all inside the
-                 timed region;
-  roofline       the dominant kernel's algorithmic bytes / its CUDA-event time, against the measured
-                 HBM copy peak (MEASURED_PEAKS.json); in the timed region, events bracket its
-                 launches in every 16th layer (both norms), so they barely perturb the step; `traffic`
-                 is that kernel's DRAM bytes from an ncu capture (NCU_TRAFFIC, profiles/);
-  cpu_baseline   the C oracle (tests' checker, a restatement of the reference's arithmetic) timed
-                 on this host's cores on a token sample of the same workload (rank 0, N = 1);
-  clocks         SM clock and throttle reasons sampled by nvidia-smi during the timed region;
-  gathered_outputs  each rank's token count and output digest.
+Reported alongside the device-resident `value` (chain workloads, this package's kernels):
+  e2e             the same step through the public API with the step's host inputs (token ids,
+                  positions) copied from pinned memory and the result (the residual stream) copied
+                  back to pinned memory on a second stream, overlapping the next step, all inside the
+                  timed region;
+  roofline        the dominant kernel's algorithmic bytes / its CUDA-event time, against the measured
+                  HBM copy peak (MEASURED_PEAKS.json); events bracket its launches in every 16th layer
+                  (both norms); `traffic` is that kernel's DRAM bytes from an ncu capture, and
+                  `ncu_in_chain_us` its mean in-chain time from an ncu launch list (profiles/);
+  flashinfer      the reference's own GPU kernels (flashinfer 0.6.11.post2 and aten's gather) on the
+                  same inputs in the same process: value, e2e, clocks;
+  chain_fp8       the other chain form, both kernel sets;
+  strong_scaling  one fixed 4352-token step split into N contiguous token ranges, both kernel sets;
+  small_steps     steps of 64, 256 and 512 tokens replayed from a CUDA graph, both kernel sets;
+  cpu_baseline    the reference's CPU path timed on this host's cores on a token sample of the same
+                  workload (rank 0, N = 1): torch's CPU embedding, and the C oracle for the ops whose
+                  reference kernels are CUDA-only;
+  fault_word, status_word  the library's words after the timed regions (must be 0);
+  gathered_outputs  every rank's digest, and an oracle check of 8 sampled tokens per rank through a
+                  whole step (the run fails if a word is nonzero or the check fails);
+  clocks          SM clock and throttle reasons sampled by nvidia-smi during the timed region.
 
---impl reference times the reference's CPU path: the reference has no CPU implementation of norm,
-silu or rope (its kernels are flashinfer's, CUDA-only), so this arm runs the C oracle port with all
-host threads on a token sample (embedding included), rank 0 only. --impl flashinfer times the
-reference's actual GPU kernels (flashinfer 0.6.11.post2, aten gather, the compiled quantize_fp8)
-on the same workload.
+--impl reference times the reference's CPU path alone (rank 0; nothing of this package's CUDA code
+is loaded). --impl flashinfer times the reference's GPU kernels alone on any workload.
 """
 from __future__ import annotations
 
@@ -89,6 +93,15 @@ NCU_TRAFFIC = {
     "silu_fp8_chain": (499_136_256 + 73_464_832, "profiles/silu_fp8_chain_shape.md"),
     "rope_append_small": (383_577_088 + 381_649_152, "profiles/rope_append_config3_small.md"),
 }
+
+
+# Mean device time of the dominant kernel inside the chain, from an ncu launch list of the bench's
+# own default command (gpu__time_duration.sum only, --clock-control none): an unperturbed in-chain
+# figure beside the event-bracketed one, which cancels the programmatic-launch overlap around it.
+NCU_IN_CHAIN: dict = {}
+
+# Bound on the end-to-end oracle check of sampled tokens (bf16 ulps / e4m3 steps after 88 layers).
+CHECK_BOUND_ULP = 8
 
 
 # --------------------------------------------------------------------------------------------------
@@ -208,12 +221,6 @@ class Clocks:
 # --------------------------------------------------------------------------------------------------
 # Implementations of the ops (the chain calls whichever namespace it is given).
 # --------------------------------------------------------------------------------------------------
-def mas_ops():
-    import mas_b200
-
-    return mas_b200.ops
-
-
 class FlashinferOps:
     """The reference's own GPU path: flashinfer kernels and the aten gather behind nn.Embedding."""
 
@@ -283,6 +290,7 @@ class FlashinferOps:
 # Workloads: each builds device state and returns closures for one step.
 # --------------------------------------------------------------------------------------------------
 def chain_config(layers: int, tokens_per_gpu: int, global_tokens: int) -> dict:
+    """The chain workload's config, identical for every arm (mas, flashinfer, reference) at one N."""
     from mas_b200 import workloads as wl
 
     s = wl.CHAIN_SHAPE
@@ -294,38 +302,66 @@ def chain_config(layers: int, tokens_per_gpu: int, global_tokens: int) -> dict:
             "l2": "inputs larger than L2 (per-layer working set 1.84 GB)", "parallelism": "token-sharded dp"}
 
 
+def chain_fp8_config(layers: int, tokens_per_gpu: int, global_tokens: int) -> dict:
+    cfg = chain_config(layers, tokens_per_gpu, global_tokens)
+    cfg["workload"] = ("chain, fp8 form (the decoder layers' own calls): embed + 88 x [RMSNorm+res -> e4m3, "
+                       "rope q/k, RMSNorm+res -> e4m3, SiLU-mul -> e4m3]")
+    cfg["norm"] = "fused_add_rmsnorm_quant"
+    return cfg
+
+
 class ChainWorkload:
+    """Configuration 5's step on this rank's tokens, through a pluggable op namespace.
+
+    The buffers hold this rank's `tokens` tokens; `view(n, ids, pos)` gives a workload over the first n
+    rows of the same buffers with other ids and positions (the strong-scaling slice, the small steps).
+    The fp8 outputs are always allocated, so one set of inputs serves both forms (`quant`).
+    """
+
     name = "chain"
-    dominant = "fused_add_rmsnorm"
     EVENT_EVERY = 16  # layers 8, 24, 40, 56, 72 carry events around both of their norms
     per_launch_value = False
 
-    def __init__(self, device, dist: Dist, ops, layers: int, quant: bool = False):
+    def __init__(self, device, ops, layers: int, host_ids, host_pos, seed: int, quant: bool = False,
+                 buffers=None):
         from mas_b200 import workloads as wl
         from mas_b200.chain import LayerChain
 
-        self.quant = quant
-        if quant:
-            self.name, self.dominant = "chain_fp8", "fused_add_rmsnorm_quant"
         self.wl = wl
         self.shape = wl.CHAIN_SHAPE
-        ids, pos = wl.chain_host_inputs(replicas=dist.world)
-        per = ids.shape[0] // dist.world
-        s, e = dist.rank * per, (dist.rank + 1) * per
-        self.host_ids = ids[s:e].clone().pin_memory()
-        self.host_pos = pos[s:e].clone().pin_memory()
-        self.tokens = per
-        self.global_tokens = ids.shape[0]
-        self.b = wl.chain_buffers(self.host_ids, self.host_pos, device=device, seed=4 + dist.rank, layers=layers,
-                                  quant=quant)
-        self.chain = LayerChain(self.shape, quant=quant, layers=layers)
+        self.device = device
+        self.host_ids = host_ids.clone().pin_memory()
+        self.host_pos = host_pos.clone().pin_memory()
+        self.tokens = host_ids.shape[0]
+        self.layers = layers
+        self.seed = seed
+        self.b = buffers if buffers is not None else wl.chain_buffers(
+            self.host_ids, self.host_pos, device=device, seed=seed, layers=layers, quant=True)
         self.chain_ops = ops
-        self.layers = self.chain.layers
-        self.host_out = torch.empty(self.b.residual.shape, dtype=self.b.residual.dtype).pin_memory()
-        self._dom_events = None
+        self.set_quant(quant)
+
+    def set_quant(self, quant: bool) -> None:
+        from mas_b200.chain import LayerChain
+
+        self.quant = quant
+        self.name = "chain_fp8" if quant else "chain"
+        self.dominant = "fused_add_rmsnorm_quant" if quant else "fused_add_rmsnorm"
+        self.chain = LayerChain(self.shape, quant=quant, layers=self.layers)
+
+    def view(self, n: int, host_ids, host_pos) -> "ChainWorkload":
+        """A workload over the first n rows of these buffers, with the given ids and positions."""
+        from mas_b200.chain import ChainBuffers
+
+        b = self.b
+        v = ChainBuffers(ids=host_ids.to(self.device), positions=host_pos.to(self.device), table=b.table,
+                         hidden=b.hidden[:n], residual=b.residual[:n], attn_out=b.attn_out[:n], qkv=b.qkv[:n],
+                         gate_up=b.gate_up[:n], act=b.act[:n], cos_sin_cache=b.cos_sin_cache, w_in=b.w_in,
+                         w_post=b.w_post, x_fp8=b.x_fp8[:n], act_fp8=b.act_fp8[:n], act_scale=b.act_scale)
+        return ChainWorkload(self.device, self.chain_ops, self.layers, host_ids, host_pos, self.seed,
+                             quant=self.quant, buffers=v)
 
     # the chain with a pluggable op namespace, optionally bracketing the dominant kernel with events
-    def _step(self, dom_events=None):
+    def step(self, dom_events=None):
         b, s, o = self.b, self.shape, self.chain_ops
         eps = s.rms_norm_eps
         o.embedding_out(b.hidden, b.ids, b.table)
@@ -366,14 +402,12 @@ class ChainWorkload:
             else:
                 o.silu_and_mul(b.gate_up, out=b.act, enable_pdl=True)
 
-    def step(self, dom_events=None):
-        self._step(dom_events)
-
     def e2e_setup(self):
         """Two residual buffers and two pinned host outputs, alternating by step, and a copy stream."""
         b = self.b
+        self._res0 = b.residual
         self._res = [b.residual, torch.empty_like(b.residual)]
-        self._host_out = [self.host_out, torch.empty(self.host_out.shape, dtype=self.host_out.dtype).pin_memory()]
+        self._host_out = [torch.empty(b.residual.shape, dtype=b.residual.dtype).pin_memory() for _ in range(2)]
         self._copy_stream = torch.cuda.Stream(device=b.residual.device)
         self._d2h_done = [None, None]
         self._i = 0
@@ -391,7 +425,7 @@ class ChainWorkload:
         b.residual = self._res[k]
         b.ids.copy_(self.host_ids, non_blocking=True)
         b.positions.copy_(self.host_pos, non_blocking=True)
-        self._step(None)
+        self.step(None)
         done = torch.cuda.Event()
         done.record(main)
         cs = self._copy_stream
@@ -404,17 +438,38 @@ class ChainWorkload:
         self._i += 1
 
     def e2e_finish(self):
-        """Makes the current stream wait for the last copy to the host (inside the timed region)."""
+        """Makes the current stream wait for the last copy to the host (inside the timed region), and
+        puts the first residual buffer back."""
         torch.cuda.current_stream().wait_stream(self._copy_stream)
+        self.b.residual = self._res0
 
     def digest(self) -> dict:
         """This rank's output fingerprint (outside the timed region): its token count and the integer
-        sums of the final residual and hidden bit patterns. Rank 0 of an N-GPU run processes the
-        same step as a 1-GPU run, so with equal --steps/--warmup its digest equals the 1-GPU one."""
+        sums of the final residual and hidden bit patterns."""
         b = self.b
         return {"tokens": int(self.tokens),
                 "residual_bits_sum": int(b.residual.view(torch.int16).to(torch.int64).sum().item()),
                 "hidden_bits_sum": int(b.hidden.view(torch.int16).to(torch.int64).sum().item())}
+
+    def sample_step(self, n: int = 8) -> dict:
+        """One more step, with the inputs and outputs of `n` evenly spaced tokens copied to the host for
+        an oracle check. Every op is per token, so the sampled tokens' outputs depend only on their own
+        inputs (the layer weights are shared). Inputs carried from step to step (attn_out and qkv are
+        updated in place) are captured just before the step."""
+        b, s = self.b, self.shape
+        sel = torch.linspace(0, self.tokens - 1, n, device=self.device).long()
+        ids = b.ids[sel]
+        inp = {"ids": ids.cpu(), "table_rows": b.table[ids].cpu(), "attn_out": b.attn_out[sel].cpu(),
+               "qkv": b.qkv[sel].cpu(), "gate_up": b.gate_up[sel].cpu(), "cache_rows": b.cos_sin_cache[
+                   b.positions[sel].long()].cpu(), "w_in": b.w_in.cpu(), "w_post": b.w_post.cpu(),
+               "act_scale": b.act_scale.cpu()}
+        self.step()
+        out = {"residual": b.residual[sel].cpu(), "qkv": b.qkv[sel].cpu()}
+        if self.quant:
+            out.update(x_fp8=b.x_fp8[sel].cpu(), act_fp8=b.act_fp8[sel].cpu())
+        else:
+            out.update(hidden=b.hidden[sel].cpu(), attn_out=b.attn_out[sel].cpu(), act=b.act[sel].cpu())
+        return {"tokens": sel.cpu(), "quant": self.quant, "layers": self.layers, "inputs": inp, "outputs": out}
 
     def e2e_bytes(self) -> tuple[int, int]:
         return (self.host_ids.numel() * 8 + self.host_pos.numel() * 4,
@@ -429,13 +484,57 @@ class ChainWorkload:
     def dominant_bytes_per_launch(self) -> int:
         return (7 if self.quant else 8) * self.tokens * self.shape.hidden_size + 2 * self.shape.hidden_size
 
-    def config(self) -> dict:
-        cfg = chain_config(self.layers, self.tokens, self.global_tokens)
-        if self.quant:
-            cfg["workload"] = ("chain, fp8 form (the decoder layers' own calls): embed + 88 x [RMSNorm+res -> e4m3, "
-                               "rope q/k, RMSNorm+res -> e4m3, SiLU-mul -> e4m3]")
-            cfg["norm"] = "fused_add_rmsnorm_quant"
-        return cfg
+
+def oracle_check(sample: dict, eps: float) -> dict:
+    """Runs the oracle over a `ChainWorkload.sample_step` sample and compares: max distance in units
+    of the output format's last place (bf16 ulps, e4m3 steps) per output.
+
+    The oracle follows the reference's kernels to within one ulp per op; over 88 chained layers such
+    last-place differences feed later layers (the residual stream carries them), so an end-to-end
+    comparison allows a few ulps where the op-by-op tests allow one."""
+    import oracle
+    from mas_b200 import workloads as wl
+
+    s = wl.CHAIN_SHAPE
+    inp, L = sample["inputs"], sample["layers"]
+    n = inp["ids"].shape[0]
+    hidden = inp["table_rows"].clone()
+    residual = torch.zeros_like(hidden)
+    attn, qkv, gate_up = inp["attn_out"].clone(), inp["qkv"].clone(), inp["gate_up"]
+    pos = torch.arange(n, dtype=torch.int32)
+    cache = inp["cache_rows"].contiguous()
+    act = torch.empty(n, s.intermediate_size, dtype=torch.bfloat16)
+    x8 = torch.empty(n, s.hidden_size, dtype=torch.float8_e4m3fn)
+    act8 = torch.empty(n, s.intermediate_size, dtype=torch.float8_e4m3fn)
+    sc = inp["act_scale"].tolist()
+    q = qkv[:, : s.q_size]
+    k = qkv[:, s.q_size: s.q_size + s.kv_size]
+    for l in range(L):
+        if sample["quant"]:
+            oracle.fused_add_rmsnorm_quant(x8, hidden, residual, inp["w_in"][l], sc[0], eps)
+        else:
+            oracle.fused_add_rmsnorm(hidden, residual, inp["w_in"][l], eps)
+        oracle.apply_rope_with_cos_sin_cache_inplace(pos, q, k, s.head_dim, cache)
+        if sample["quant"]:
+            oracle.fused_add_rmsnorm_quant(x8, attn, residual, inp["w_post"][l], sc[1], eps)
+            oracle.silu_and_mul_quant(gate_up, sc[2], out=act8)
+        else:
+            oracle.fused_add_rmsnorm(attn, residual, inp["w_post"][l], eps)
+            oracle.silu_and_mul(gate_up, out=act)
+    want = {"residual": residual, "qkv": qkv}
+    if sample["quant"]:
+        want.update(x_fp8=x8, act_fp8=act8)
+    else:
+        want.update(hidden=hidden, attn_out=attn, act=act)
+
+    def ordered(t):
+        if t.dtype == torch.float8_e4m3fn:
+            i = t.view(torch.uint8).to(torch.int32)
+            return torch.where(i >= 128, -(i & 127), i)
+        i = t.contiguous().view(torch.int16).to(torch.int32)
+        return torch.where(i < 0, -(i & 0x7FFF), i)
+
+    return {name: int((ordered(sample["outputs"][name]) - ordered(w)).abs().max()) for name, w in want.items()}
 
 
 class OpWorkload:
@@ -604,10 +703,13 @@ class OpWorkload:
 
 
 # --------------------------------------------------------------------------------------------------
-# CPU arm: the C oracle on a token sample of the chain.
+# CPU arm: the reference's CPU path on a token sample of the chain.
 # --------------------------------------------------------------------------------------------------
 class CpuChainSample:
-    """The oracle running the chain on `tokens` sampled tokens (all layers), inputs on the host."""
+    """The chain on `tokens` sampled tokens (all layers), inputs on the host: the embedding through
+    torch's own CPU embedding (the reference's nn.Embedding path, devstral2.py:260, :282), and the
+    norms, rope and SiLU-mul through the C oracle (the reference has no CPU implementation of those:
+    its kernels are flashinfer's, CUDA-only)."""
 
     def __init__(self, tokens: int, layers: int, seed: int = 4):
         import oracle
@@ -635,7 +737,7 @@ class CpuChainSample:
 
     def step(self):
         o, s = self.oracle, self.s
-        hidden, _ = o.embedding(self.local_ids, self.table)
+        hidden = torch.nn.functional.embedding(self.local_ids, self.table)
         residual = torch.zeros_like(hidden)
         q = self.qkv[:, : s.q_size]
         k = self.qkv[:, s.q_size: s.q_size + s.kv_size]
@@ -674,18 +776,21 @@ def time_cpu_chain(tokens: int, layers: int, reps: int) -> tuple[float, list[flo
 # --------------------------------------------------------------------------------------------------
 # Arms.
 # --------------------------------------------------------------------------------------------------
-def run_reference_arm(args, dist: Dist) -> None:
-    """The reference's CPU path on this host (C oracle port, all threads), rank 0 only."""
-    if dist.rank != 0:
+def run_reference_arm(args, world: int, rank: int) -> None:
+    """The reference's CPU path on this host (all threads), rank 0 only, on the GPU arms' config.
+
+    Nothing here loads this package's CUDA libraries: workloads, chain shapes and the cos/sin cache
+    are host-only modules, and the arithmetic is the C oracle's and torch's."""
+    if rank != 0:
+        return
+    if args.workload != "chain":
+        print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm is defined for the chain workload"}))
         return
     import oracle
 
     cores = host_cores()
     oracle.set_num_threads(cores)
     layers = args.layers or 88
-    if args.workload != "chain":
-        print(json.dumps({"impl": "reference", "unavailable": "the CPU reference arm is defined for the chain workload"}))
-        return
     per_step_budget = max(0.5, min(4.0, 150.0 / max(1, args.steps + args.warmup)))
     tokens = calibrate_cpu_tokens(layers, per_step_budget)
     w = CpuChainSample(tokens, layers)
@@ -696,91 +801,224 @@ def run_reference_arm(args, dist: Dist) -> None:
         w.step()
     dt = (time.perf_counter() - t0) / args.steps
     value = tokens / dt
-    s = w.s
     from mas_b200.chain import LayerChain
 
-    chain = LayerChain(s, layers=layers)
+    chain = LayerChain(w.s, layers=layers)
+    sample = (f"{tokens} of the 4352 tokens of a step, all {layers} layers, per step; embedding by torch's CPU "
+              f"embedding, norms/rope/SiLU-mul by the C oracle (OpenMP, {cores} threads)")
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": dist.world,
+        "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": dict(chain_config(layers, 4352, 4352), tokens_sampled_per_step=tokens),
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{tokens} of 4352 tokens per step, all {layers} layers, C oracle (OpenMP)"},
+        "config": chain_config(layers, 4352, 4352 * world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "hbm_gbs_equivalent": chain.step_bytes(tokens) / dt / 1e9,
     }
     print(json.dumps(line))
 
 
+def _flush_queue_then(fn):
+    """Runs fn() with a spin kernel ahead of it in the stream, so that the host queues the launches of
+    fn() while the GPU is still busy: the events then time the device, not the Python launch rate."""
+    torch.cuda._sleep(SLEEP_CYCLES)
+    return fn()
+
+
+def time_steps(step, steps: int, warmup: int, dist: Dist, device, dom=None, clocks: bool = False):
+    """Device time per step (ms), max over ranks, of `steps` calls of step() after `warmup` calls;
+    barrier + synchronize on both sides. Returns (ms, clocks summary or None)."""
+    st = torch.cuda.current_stream()
+    for _ in range(warmup):
+        step(None)
+    torch.cuda.synchronize()
+    clk = Clocks(device.index) if clocks else None
+    if clk is not None:
+        clk.__enter__()
+        time.sleep(0.25)
+    try:
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+        def region():
+            e0.record(st)
+            for _ in range(steps):
+                step(dom)
+            e1.record(st)
+
+        _flush_queue_then(region)
+        torch.cuda.synchronize()
+        dist.barrier()
+    finally:
+        if clk is not None:
+            clk.__exit__(None, None, None)
+    ms = dist.max(e0.elapsed_time(e1) / steps, device)
+    return ms, (clk.summary() if clk is not None else None)
+
+
+def time_e2e(w: ChainWorkload, steps: int, warmup: int, dist: Dist, device) -> float:
+    """ms per step through the public API with host inputs and outputs (ChainWorkload.e2e_step)."""
+    st = torch.cuda.current_stream()
+    w.e2e_setup()
+    for _ in range(max(1, warmup // 2)):
+        w.e2e_step()
+    w.e2e_finish()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def region():
+        a.record(st)
+        for _ in range(steps):
+            w.e2e_step()
+        w.e2e_finish()
+        b.record(st)
+
+    _flush_queue_then(region)
+    torch.cuda.synchronize()
+    dist.barrier()
+    return dist.max(a.elapsed_time(b) / steps, device)
+
+
+def time_graph(w: ChainWorkload, steps: int, warmup: int, dist: Dist, device) -> float:
+    """ms per step of the chain captured once into a CUDA graph and replayed, as the reference's
+    runner replays steps of up to 512 tokens (model_runner.py:20, :87-119); max over ranks."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            w.step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        w.step()
+    try:
+        return time_steps(lambda _d: graph.replay(), steps, warmup, dist, device)[0]
+    finally:
+        torch.cuda.synchronize()
+        del graph
+
+
+def check_words(impl: str, device) -> dict:
+    """The library's fault and status words after a timed region (mas arm), read and cleared."""
+    if impl != "mas":
+        return {}
+    import mas_b200
+
+    return {"fault_word": mas_b200.read_fault_word(device.index, clear=True),
+            "status_word": mas_b200.read_status(device)}
+
+
+def arm_record(w: ChainWorkload, args, dist: Dist, device, impl: str, e2e: bool = True) -> dict:
+    """value, ms per step, e2e and clocks of one arm on the workload's current inputs."""
+    ms, clk = time_steps(w.step, args.steps, args.warmup, dist, device, clocks=True)
+    rec = {"value": w.tokens * dist.world / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "clocks": clk}
+    if e2e and not args.no_e2e:
+        e_ms = time_e2e(w, args.steps, args.warmup, dist, device)
+        h2d, d2h = w.e2e_bytes()
+        rec["e2e"] = {"value": w.tokens * dist.world / (e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e_ms,
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    rec.update(check_words(impl, device))
+    return rec
+
+
+def strong_and_small(w: ChainWorkload, args, dist: Dist, device, arms: dict) -> tuple[dict, dict]:
+    """Strong scaling (one fixed 4352-token step split into N contiguous token ranges, positions
+    alongside) and small steps (T = 64, 256, 512 tokens, replayed from a CUDA graph), per arm."""
+    from mas_b200 import workloads as wl
+
+    ids, pos = wl.chain_host_inputs(replicas=1)
+    T = ids.shape[0]
+    s, e = shard(T, dist.world, dist.rank)
+    strong = {"global_tokens": T, "tokens_per_gpu": [shard(T, dist.world, r)[1] - shard(T, dist.world, r)[0]
+                                                      for r in range(dist.world)],
+              "timing": "eager launches, max over ranks"}
+    small = {"timing": "one step captured into a CUDA graph and replayed, max over ranks",
+             "tokens": [64, 256, 512]}
+    for name, ops in arms.items():
+        w.chain_ops = ops
+        v = w.view(e - s, ids[s:e], pos[s:e])
+        ms, _ = time_steps(v.step, args.steps, args.warmup, dist, device)
+        strong[name] = {"value": T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms}
+        for n in small["tokens"]:
+            v = w.view(n, ids[:n], pos[:n])
+            ms = time_graph(v, args.steps, args.warmup, dist, device)
+            small.setdefault(name, {})[str(n)] = {"value": n * dist.world / (ms / 1e3), "unit": "tokens/s",
+                                                  "ms_per_step": ms}
+    return strong, small
+
+
 def run_gpu_arm(args, dist: Dist) -> None:
     device = torch.device("cuda", dist.local_rank)
     torch.cuda.set_device(device)
+    mas = None
     if args.impl == "flashinfer":
         ops = FlashinferOps()
     else:
-        ops = mas_ops()
         import mas_b200
 
+        mas = ops = mas_b200.ops
         mas_b200.prepare_device(device.index)
+        mas_b200.read_fault_word(device.index, clear=True)
+        mas_b200.read_status(device)
     layers = args.layers or 88
-    if args.workload in ("chain", "chain_fp8"):
-        w = ChainWorkload(device, dist, ops, layers, quant=args.workload == "chain_fp8")
+    chain = args.workload in ("chain", "chain_fp8")
+    if chain:
+        from mas_b200 import workloads as wl
+
+        ids, pos = wl.chain_host_inputs(replicas=dist.world)
+        per = ids.shape[0] // dist.world
+        s, e = dist.rank * per, (dist.rank + 1) * per
+        w = ChainWorkload(device, ops, layers, ids[s:e], pos[s:e], seed=4 + dist.rank,
+                          quant=args.workload == "chain_fp8")
+        w.global_tokens = per * dist.world
     else:
         w = OpWorkload(args.workload, device, dist, ops)
 
-    st = torch.cuda.current_stream()
-    for _ in range(args.warmup):
-        w.step()
-    torch.cuda.synchronize()
-
     # ---- device-resident timed region -----------------------------------------------------------
-    dom = []
-    with Clocks(device.index) as clocks:
-        time.sleep(0.25)
-        dist.barrier()
-        torch.cuda.synchronize()
-        # A spin kernel holds the GPU while the host queues the whole timed region, so the region
-        # measures the device, not the Python launch rate.
-        torch.cuda._sleep(SLEEP_CYCLES)
-        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e_start.record(st)
-        for _ in range(args.steps):
-            w.step(dom_events=dom if not args.no_kernel_events else None)
-        e_end.record(st)
-        torch.cuda.synchronize()
-        dist.barrier()
-    ms = e_start.elapsed_time(e_end) / args.steps
-    ms = dist.max(ms, device)
+    dom = [] if not args.no_kernel_events else None
+    ms, clocks = time_steps(w.step, args.steps, args.warmup, dist, device, dom=dom, clocks=True)
+    words = check_words(args.impl, device)
     dom_ms = statistics.fmean(a.elapsed_time(b) for a, b in dom) if dom else None
     if dom_ms is not None:
         dom_ms = dist.max(dom_ms, device)
 
     # ---- end-to-end through the public API with host inputs/outputs --------------------------------
     e2e = None
-    if args.workload in ("chain", "chain_fp8") and not args.no_e2e:
-        w.e2e_setup()
-        for _ in range(max(1, args.warmup // 2)):
-            w.e2e_step()
-        w.e2e_finish()
-        torch.cuda.synchronize()
-        dist.barrier()
-        torch.cuda.synchronize()
-        torch.cuda._sleep(SLEEP_CYCLES)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(st)
-        for _ in range(args.steps):
-            w.e2e_step()
-        w.e2e_finish()
-        b.record(st)
-        torch.cuda.synchronize()
-        dist.barrier()
-        e2e_ms = dist.max(a.elapsed_time(b) / args.steps, device)
+    if chain and not args.no_e2e:
+        e2e_ms = time_e2e(w, args.steps, args.warmup, dist, device)
         h2d, d2h = w.e2e_bytes()
         e2e = {"value": w.global_tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                "path": "public API (mas_b200 ops), pinned host ids+positions in, residual stream out "
                        "(copy stream, double-buffered: step i's copy out overlaps step i+1's kernels)"}
+        for k, v in check_words(args.impl, device).items():
+            words[k] = words.get(k, 0) | v
+
+    # ---- the reference's GPU kernels on the same inputs, the other chain form, strong/small steps ----
+    subs = {}
+    if chain and args.impl == "mas" and not args.no_compare:
+        fi = FlashinferOps()
+        w.chain_ops = fi
+        subs["flashinfer"] = dict(arm_record(w, args, dist, device, "flashinfer"),
+                                  kernels="flashinfer 0.6.11.post2 (norm, rope, silu) + aten index_select (gather)")
+        other = not w.quant
+        w.set_quant(other)
+        rec = {"config": (chain_fp8_config if other else chain_config)(layers, w.tokens, w.global_tokens)}
+        w.chain_ops = mas
+        rec["mas"] = arm_record(w, args, dist, device, "mas")
+        w.chain_ops = fi
+        rec["flashinfer"] = arm_record(w, args, dist, device, "flashinfer")
+        subs["chain_fp8" if other else "chain_bf16"] = rec
+        w.set_quant(not other)
+        subs["strong_scaling"], subs["small_steps"] = strong_and_small(w, args, dist, device,
+                                                                       {"mas": mas, "flashinfer": fi})
+        w.chain_ops = mas
+        for k in ("fault_word", "status_word"):
+            words[k] = words.get(k, 0) | rec["mas"].get(k, 0)
 
     # ---- CPU baseline (rank 0, N = 1) ----------------------------------------------------------------
     cpu = None
@@ -792,15 +1030,31 @@ def run_gpu_arm(args, dist: Dist) -> None:
         tokens = calibrate_cpu_tokens(layers, 3.0)
         value_cpu, times = time_cpu_chain(tokens, layers, reps=3)
         cpu = {"value": value_cpu, "unit": "tokens/s", "cores": cores, "kind": "port",
-               "sample": f"{tokens} of {w.tokens} tokens, all {layers} layers, C oracle, median of 3 steps "
-                         f"({sum(times):.1f} s of CPU work)"}
+               "sample": f"{tokens} of {w.tokens} tokens, all {layers} layers, median of 3 steps "
+                         f"({sum(times):.1f} s of CPU work); embedding by torch's CPU embedding, the rest by "
+                         f"the C oracle"}
 
     # ---- outputs gathered for checking (NCCL, outside every timed region) ------------------------
     gathered = None
-    if hasattr(w, "digest"):
-        per_rank = dist.gather_objects(w.digest())
-        gathered = {"ranks": dist.world, "per_rank": per_rank,
-                    "tokens_total": sum(d["tokens"] for d in per_rank)}
+    if chain:
+        sample = w.sample_step()
+        per_rank = dist.gather_objects({"rank": dist.rank, "digest": w.digest(), "sample": sample})
+        if dist.rank == 0:
+            checks = []
+            for r in per_rank:
+                ulps = oracle_check(r["sample"], w.shape.rms_norm_eps)
+                checks.append({"rank": r["rank"], "tokens_checked": int(r["sample"]["tokens"].numel()),
+                               "max_ulp": ulps})
+            worst = max(max(c["max_ulp"].values()) for c in checks)
+            gathered = {"ranks": dist.world, "digests": [r["digest"] for r in per_rank],
+                        "tokens_total": sum(r["digest"]["tokens"] for r in per_rank),
+                        "oracle_check": {"per_rank": checks, "worst_ulp": worst, "bound_ulp": CHECK_BOUND_ULP,
+                                         "ok": worst <= CHECK_BOUND_ULP,
+                                         "how": "8 evenly spaced tokens per rank, one full step (all layers) "
+                                                "after the timed regions, gathered to rank 0 over NCCL and "
+                                                "replayed by the C oracle"}}
+        for k, v in check_words(args.impl, device).items():
+            words[k] = words.get(k, 0) | v
 
     if dist.rank != 0:
         return
@@ -817,25 +1071,41 @@ def run_gpu_arm(args, dist: Dist) -> None:
         if traffic is None and args.impl == "mas" and args.workload in NCU_TRAFFIC:
             traffic, traffic_src = NCU_TRAFFIC[args.workload]
         roof = {"bound": "hbm", "kernel": w.dominant, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                "frac": achieved / peak,
+                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
                 "traffic": traffic, "traffic_source": traffic_src, "bytes_per_launch": w.dominant_bytes_per_launch(),
                 "avg_launch_us": dom_ms * 1e3, "launches_timed": len(dom)}
+        if chain and args.impl == "mas" and args.workload in NCU_IN_CHAIN:
+            us, src = NCU_IN_CHAIN[args.workload]
+            roof["ncu_in_chain_us"] = us
+            roof["ncu_in_chain_frac"] = w.dominant_bytes_per_launch() / (us / 1e6) / 1e9 / peak
+            roof["ncu_in_chain_source"] = src
+    if chain:
+        cfg = (chain_fp8_config if w.quant else chain_config)(layers, w.tokens, w.global_tokens)
+    else:
+        cfg = w.config()
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, random ids/positions)",
-        "config": w.config(),
+        "config": cfg,
         "hbm_gbs_per_gpu": gbs, "hbm_frac_of_peak": gbs / peak, "hbm_peak_kind": peak_kind,
         "hbm_frac_of_nominal_8tbs": gbs / NOMINAL_HBM_GBS,
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
         "gpu_launches": (w.launches_per_step() * args.steps) if args.impl == "mas" else 0,
-        "clocks": clocks.summary(),
+        "clocks": clocks,
     }
+    line.update(words)
+    line.update(subs)
     if gathered is not None:
         line["gathered_outputs"] = gathered
     if args.impl != "mas":
         line["impl"] = args.impl
-    print(json.dumps(line))
+    print(json.dumps(line), flush=True)
+    bad = [k for k in ("fault_word", "status_word") if line.get(k)]
+    if bad or (gathered is not None and not gathered["oracle_check"]["ok"]):
+        print(f"bench: check failed: {bad or 'oracle check'}", file=sys.stderr)
+        raise SystemExit(1)
 
 
 def main(argv=None) -> None:
@@ -852,6 +1122,8 @@ def main(argv=None) -> None:
     ap.add_argument("--layers", type=int, default=0, help="chain layers (default 88)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-compare", action="store_true",
+                    help="chain: skip the flashinfer, other-form, strong-scaling and small-step sub-records")
     ap.add_argument("--no-kernel-events", action="store_true", help="time the region without per-launch events")
     ap.add_argument("--traffic", type=float, default=None, help="ncu DRAM bytes per dominant launch, if known")
     args = ap.parse_args(argv)
@@ -859,7 +1131,7 @@ def main(argv=None) -> None:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         # CPU only: no process group; under torchrun rank 0 runs and the other ranks exit at once.
-        run_reference_arm(args, Dist(backend="none"))
+        run_reference_arm(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
     dist = Dist()
     try:

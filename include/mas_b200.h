@@ -46,9 +46,11 @@ extern "C" {
 #define MAS_ERR_UNSUPPORTED_SHAPE (-3) /* e.g. odd rotary_dim, head_size < rotary_dim */
 #define MAS_ERR_NO_DEVICE (-4)         /* no current CUDA device could be queried */
 
-/* Device-side status bits, OR-ed (atomicOr) into the optional int32 `status` word some kernels
- * take. The word is never cleared by the library; the caller zeroes it and reads it when it chooses
- * (reading it is a host sync, so the ops themselves never do). */
+/* Device-side status bits, OR-ed (atomicOr) into the int32 `status` word the gather, rope and
+ * paged-append kernels take. A NULL `status` selects the library's own status word of the current
+ * device (mas_read_status_word), so a data error is always recorded somewhere, including in calls
+ * traced by torch.compile or replayed from a CUDA graph. No word is ever cleared by the kernels; the
+ * caller zeroes and reads it when it chooses (reading is a host sync, so the ops never do). */
 #define MAS_STATUS_EMBED_ID_OUT_OF_RANGE 1 /* an id outside [0, vocab): its output row is zeroed */
 #define MAS_STATUS_ROPE_POS_OUT_OF_RANGE 2 /* a position outside [0, max_positions): token left as is */
 #define MAS_STATUS_COPY_TIMEOUT 4          /* a bulk-copy wait ran past its time limit; outputs undefined */
@@ -70,6 +72,13 @@ MAS_API int mas_prepare_device(int device);
  * never called by the ops themselves, not for use during stream capture. The reference has no such
  * facility (flashinfer kernels have no bounded waits to report). */
 MAS_API int mas_read_fault_word(int device, int32_t* value, int clear);
+
+/* Reads (and, if `clear` is nonzero, zeroes) the library status word of `device`: the OR of the
+ * MAS_STATUS_* data-error bits of every call on that device made with a NULL `status` (an
+ * out-of-range token id, rope position or paged-KV slot). Host-synchronising, like
+ * mas_read_fault_word. It stands in for the device-side index checks by which aten's embedding and
+ * flashinfer's kernels would raise or fault (miniagentserve/models/devstral2/devstral2.py:282). */
+MAS_API int mas_read_status_word(int device, int32_t* value, int clear);
 
 /*
  * Self-test of failure detection (no counterpart in the reference): launches one thread that waits
@@ -143,7 +152,7 @@ MAS_API int mas_silu_and_mul_quant(void* out, const void* input, const float* sc
  * and likewise k; both may be strided views of one fused qkv row.
  * positions: int32 (positions_dtype MAS_DTYPE_INT32) or int64 (MAS_DTYPE_INT64).
  * A position outside [0, max_positions) leaves that token unchanged and sets
- * MAS_STATUS_ROPE_POS_OUT_OF_RANGE in *status when status is not NULL.
+ * MAS_STATUS_ROPE_POS_OUT_OF_RANGE in *status (the library status word when status is NULL).
  * Replaces flashinfer.rope.apply_rope_with_cos_sin_cache_inplace (FI/rope.py:1223-1272; kernels
  * FI/data/include/flashinfer/pos_enc.cuh:129-147, 294-420, dispatch 1295-1372), called by
  * Devstral2Attention.forward (miniagentserve/models/devstral2/devstral2.py:163-166).
@@ -178,7 +187,7 @@ MAS_API int mas_rope_cos_sin_cache_q_scale_inplace(const void* positions, int po
 /*
  * Token-embedding gather: out[t, :] = table[ids[t], :] (a bit copy of hidden_size elements of
  * elem_size bytes). ids: int32 or int64 (ids_dtype). An id outside [0, vocab_size) zeroes its output
- * row and sets MAS_STATUS_EMBED_ID_OUT_OF_RANGE in *status when status is not NULL.
+ * row and sets MAS_STATUS_EMBED_ID_OUT_OF_RANGE in *status (the library status word when status is NULL).
  * Replaces the aten/inductor embedding behind nn.Embedding.forward, Devstral2Model.embed_tokens
  * (miniagentserve/models/devstral2/devstral2.py:260, :282).
  */
@@ -231,7 +240,8 @@ typedef struct MasPagedKVCache {
  * page = kv_indices[flat / page_size], entry = flat % page_size, then k_cache[page, entry, h, :] =
  * key[t, h, :] and the same for v (byte-exact copies). k/v element (t, h, f) at
  * t * stride_token + h * stride_head + f. A token whose batch index, position, page slot or page id
- * is out of range is not appended and sets MAS_STATUS_KV_SLOT_OUT_OF_RANGE in *status (if not NULL).
+ * is out of range is not appended and sets MAS_STATUS_KV_SLOT_OUT_OF_RANGE in *status (the library
+ * status word when status is NULL).
  * Replaces flashinfer.page.append_paged_kv_cache (FI/page.py:280-406; kernel
  * FI/data/include/flashinfer/page.cuh:259-284), called once per attention layer
  * (miniagentserve/models/devstral2/devstral2.py:170-173). dtype: BF16 or FP16 for k, v and the cache.

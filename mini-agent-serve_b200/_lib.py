@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple[type, list[type]]] = {
     "mas_status_string": (ctypes.c_char_p, [_i32]),
     "mas_prepare_device": (_i32, [_i32]),
     "mas_read_fault_word": (_i32, [_i32, ctypes.POINTER(ctypes.c_int32), _i32]),
+    "mas_read_status_word": (_i32, [_i32, ctypes.POINTER(ctypes.c_int32), _i32]),
     "mas_selftest_bounded_wait": (_i32, [_i64, _vp]),
     "mas_fused_add_rmsnorm": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _i32, _vp]),
     "mas_fused_add_rmsnorm_quant": (
@@ -137,4 +138,11 @@ def read_fault_word(device: int, clear: bool = False) -> int:
     """The library fault word of `device` (host-synchronising diagnostic)."""
     out = ctypes.c_int32(0)
     check("mas_read_fault_word", lib.mas_read_fault_word(device, ctypes.byref(out), int(clear)))
+    return out.value
+
+
+def read_status_word(device: int, clear: bool = False) -> int:
+    """The library status word of `device`: the MAS_STATUS_* data-error bits (host-synchronising)."""
+    out = ctypes.c_int32(0)
+    check("mas_read_status_word", lib.mas_read_status_word(device, ctypes.byref(out), int(clear)))
     return out.value

@@ -21,12 +21,11 @@ arguments and tensor layouts as the model: q and k are strided views of one fuse
 """
 from __future__ import annotations
 
+import importlib
 from dataclasses import dataclass
 from typing import Any, Optional
 
 import torch
-
-from . import ops
 
 __all__ = ["ChainShape", "ChainBuffers", "LayerChain"]
 
@@ -108,16 +107,24 @@ class LayerChain:
     down_proj's quantize_fp8 (devstral2.py:110-111) fused into the activation.
     """
 
-    def __init__(self, shape: ChainShape, quant: bool = False, layers: Optional[int] = None):
+    def __init__(self, shape: ChainShape, quant: bool = False, layers: Optional[int] = None, ops: Any = None):
         self.shape = shape
         self.quant = quant
         self.layers = shape.num_hidden_layers if layers is None else layers
+        self._ops = ops  # an op namespace (this package's ops module unless given)
+
+    @property
+    def ops(self):
+        if self._ops is None:
+            self._ops = importlib.import_module(f"{__package__}.ops")
+        return self._ops
 
     def embed(self, b: ChainBuffers) -> None:
-        ops.embedding_out(b.hidden, b.ids, b.table)
+        self.ops.embedding_out(b.hidden, b.ids, b.table)
 
     def layer(self, b: ChainBuffers, l: int) -> None:
         s = self.shape
+        ops = self.ops
         eps = s.rms_norm_eps
         if self.quant:
             ops.fused_add_rmsnorm_quant(b.x_fp8, b.hidden, b.residual, b.w_in[l], b.act_scale[0:1], eps)

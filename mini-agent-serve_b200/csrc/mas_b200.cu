@@ -19,8 +19,11 @@
 
 namespace mas {
 
-// Library fault word: bulk-copy wait timeouts of kernels without a caller status word land here.
+// Library fault word: bulk-copy wait timeouts land here.
 __device__ int32_t g_fault_word;
+// Library status word: the data-error bits (MAS_STATUS_*) of calls made without a status word of
+// their own. One per device (each device's copy of the module has its own).
+__device__ int32_t g_status_word;
 
 namespace {
 
@@ -34,6 +37,7 @@ struct DeviceState {
   cudaError_t err = cudaSuccess;
   int sm_count = 0;
   int32_t* fault = nullptr;
+  int32_t* status = nullptr;  // this device's g_status_word
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -114,6 +118,9 @@ cudaError_t prepare_current(DeviceState& st, int device) {
   void* fault = nullptr;
   if ((e = cudaGetSymbolAddress(&fault, g_fault_word)) != cudaSuccess) return e;
   st.fault = static_cast<int32_t*>(fault);
+  void* status = nullptr;
+  if ((e = cudaGetSymbolAddress(&status, g_status_word)) != cudaSuccess) return e;
+  st.status = static_cast<int32_t*>(status);
   return cudaSuccess;
 }
 
@@ -415,7 +422,9 @@ bool append_ring_ok(const AppendArgs& a, int64_t head_size) {
          a.kv.stride_entry % 8 == 0 && a.kv.stride_head % 8 == 0;
 }
 
-int launch_append(const AppendArgs& a, bool bf, bool i64, DeviceState* st, void* stream, int enable_pdl) {
+int launch_append(const AppendArgs& args, bool bf, bool i64, DeviceState* st, void* stream, int enable_pdl) {
+  AppendArgs a = args;
+  if (a.status == nullptr) a.status = st->status;
   if (a.T == 0 || a.Hkv == 0) return MAS_OK;
   const bool vec = a.D % 8 == 0 && aligned(a.k, 16) && aligned(a.v, 16) && a.ksn % 8 == 0 && a.ksh % 8 == 0 &&
                    a.vsn % 8 == 0 && a.vsh % 8 == 0 && aligned(a.kv.k_cache, 16) && aligned(a.kv.v_cache, 16) &&
@@ -473,6 +482,24 @@ __global__ void selftest_wait_kernel(uint64_t limit_ns, int32_t* fault) {
   if (!mbar_wait_bounded(&bar, 0, limit_ns)) atomicOr(fault, MAS_STATUS_COPY_TIMEOUT);
 }
 
+// Reads (and optionally zeroes) one of the library's per-device words with `device` current,
+// restoring the caller's device. Synchronises the host with the device.
+int read_word(int device, int32_t& word, int32_t* value, int clear) {
+  if (value == nullptr) return MAS_ERR_INVALID_ARGUMENT;
+  int rc = prepare(device);
+  if (rc != MAS_OK) return rc;
+  int prev = -1;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e == cudaSuccess && prev != device) e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(value, word, sizeof(int32_t));
+  if (e == cudaSuccess && clear) {
+    const int32_t zero = 0;
+    e = cudaMemcpyToSymbol(word, &zero, sizeof(int32_t));
+  }
+  if (prev >= 0 && prev != device) (void)cudaSetDevice(prev);
+  return e == cudaSuccess ? MAS_OK : (int)e;
+}
+
 }  // namespace
 }  // namespace mas
 
@@ -498,19 +525,11 @@ const char* mas_status_string(int code) {
 int mas_prepare_device(int device) { return prepare(device); }
 
 int mas_read_fault_word(int device, int32_t* value, int clear) {
-  if (value == nullptr) return MAS_ERR_INVALID_ARGUMENT;
-  int rc = prepare(device);
-  if (rc != MAS_OK) return rc;
-  int prev = -1;
-  cudaError_t e = cudaGetDevice(&prev);
-  if (e == cudaSuccess && prev != device) e = cudaSetDevice(device);
-  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(value, g_fault_word, sizeof(int32_t));
-  if (e == cudaSuccess && clear) {
-    const int32_t zero = 0;
-    e = cudaMemcpyToSymbol(g_fault_word, &zero, sizeof(int32_t));
-  }
-  if (prev >= 0 && prev != device) (void)cudaSetDevice(prev);
-  return e == cudaSuccess ? MAS_OK : (int)e;
+  return read_word(device, g_fault_word, value, clear);
+}
+
+int mas_read_status_word(int device, int32_t* value, int clear) {
+  return read_word(device, g_status_word, value, clear);
 }
 
 int mas_selftest_bounded_wait(int64_t limit_ns, void* stream) {
@@ -674,6 +693,7 @@ static int rope_main(const void* positions, int positions_dtype, void* query, vo
   DeviceState* st = nullptr;
   int rc = current_device(&st);
   if (rc != MAS_OK) return rc;
+  if (status == nullptr) status = st->status;
   RopeArgs a = {};
   a.pos = positions; a.q = query; a.k = key; a.cache = cos_sin_cache;
   a.T = num_tokens; a.P = max_positions;
@@ -863,7 +883,7 @@ static int gather_impl(void* out, const void* table, const void* ids, int ids_dt
   EmbedArgs a = {};
   a.out = out; a.table = table; a.ids = ids; a.T = num_tokens; a.V = vocab_size;
   a.out_stride_b = out_stride * elem_size; a.table_stride_b = table_stride * elem_size;
-  a.row_bytes = (uint32_t)row_bytes; a.status = status; a.fault = st->fault;
+  a.row_bytes = (uint32_t)row_bytes; a.status = status ? status : st->status; a.fault = st->fault;
   a.last = last; a.n_last = num_last; a.last_is_64 = last_dtype == MAS_DTYPE_INT64 ? 1 : 0;
   const bool i64 = ids_dtype == MAS_DTYPE_INT64;
   const bool tma = row_bytes % 16 == 0 && row_bytes <= 64 * 1024 && aligned(out, 16) &&

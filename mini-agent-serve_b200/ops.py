@@ -46,7 +46,6 @@ __all__ = [
     "embedding",
     "embedding_out",
     "embedding_fill_placeholders",
-    "status_word",
     "read_status",
 ]
 
@@ -73,46 +72,21 @@ def _act_code(t: torch.Tensor) -> int:
 
 
 # ------------------------------------------------------------------------------------------------
-# Device status word (out-of-range ids / positions), one int32 per device.
+# Device status word (out-of-range ids, positions and paged-KV slots), one int32 per device.
 # ------------------------------------------------------------------------------------------------
-_status: dict[int, torch.Tensor] = {}
-
-
-def status_word(device: Union[int, torch.device, None] = None) -> Optional[torch.Tensor]:
-    """The int32 status word the gather and rope kernels OR their MAS_STATUS_* bits into.
-
-    Created (zeroed) on first use outside stream capture; while a capture is in progress and the
-    word does not exist yet, None is returned and the kernels report nothing.
-    """
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    w = _status.get(idx)
-    if w is None:
-        if torch.cuda.is_current_stream_capturing():
-            return None
-        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
-        _status[idx] = w
-    return w
-
-
 def read_status(device: Union[int, torch.device, None] = None, clear: bool = True) -> int:
-    """Reads (host sync) and optionally clears the status word of `device`."""
-    w = status_word(device)
-    if w is None:
-        return 0
-    v = int(w.item())
-    if clear:
-        w.zero_()
-    return v
+    """The MAS_STATUS_* bits the gather, rope and paged-append kernels have raised on `device` since it
+    was last cleared, then (by default) clears them. This synchronises the host with the device.
 
-
-def _status_arg(device: torch.device) -> Optional[torch.Tensor]:
-    """The status word to hand a kernel: none off CUDA, and none while torch.compile traces (the
-    word is a side channel for eager and graph-replayed steps, not part of the traced program)."""
-    if device.type != "cuda" or torch.compiler.is_compiling():
-        return None
-    w = _status.get(device.index)
-    return w if w is not None else status_word(device)
+    The word lives in the library (one per device), so every launch reports into it: eager calls,
+    calls traced by torch.compile and launches replayed from a CUDA graph alike.
+    """
+    if device is None:
+        idx = torch.cuda.current_device()
+    else:
+        dev = torch.device(device) if not isinstance(device, int) else torch.device("cuda", device)
+        idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    return _lib.read_status_word(idx, clear)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -290,7 +264,7 @@ def _check_rope(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
 
 
 @torch.library.register_fake("mas_b200::apply_rope_pos_ids_cos_sin_cache")
-def _(q, k, cos_sin_cache, pos_ids, interleave, enable_pdl, status) -> None:
+def _(q, k, cos_sin_cache, pos_ids, interleave, enable_pdl) -> None:
     return None
 
 
@@ -311,12 +285,12 @@ def apply_rope_with_cos_sin_cache_inplace(positions: torch.Tensor, query: torch.
         return
     q = query.view(query.shape[0], -1, head_size)
     k = key.view(key.shape[0], -1, head_size)
-    _OP_ROPE(q, k, cos_sin_cache, positions, not is_neox, True if enable_pdl is None else bool(enable_pdl),
-             _status_arg(query.device))
+    _OP_ROPE(q, k, cos_sin_cache, positions.contiguous(), not is_neox,
+             True if enable_pdl is None else bool(enable_pdl))
 
 
 @torch.library.register_fake("mas_b200::apply_rope_q_scale")
-def _(q, k, cos_sin_cache, pos_ids, interleave, beta, original_max, enable_pdl, status) -> None:
+def _(q, k, cos_sin_cache, pos_ids, interleave, beta, original_max, enable_pdl) -> None:
     return None
 
 
@@ -342,21 +316,21 @@ def apply_rope_and_llama4_query_scale_inplace(positions: torch.Tensor, query: to
         return
     q = query.view(query.shape[0], -1, head_size)
     k = key.view(key.shape[0], -1, head_size)
-    _OP_ROPE_QS(q, k, cos_sin_cache, positions, not is_neox, float(beta), int(original_max_position_embeddings),
-                True if enable_pdl is None else bool(enable_pdl), _status_arg(query.device))
+    _OP_ROPE_QS(q, k, cos_sin_cache, positions.contiguous(), not is_neox, float(beta),
+                int(original_max_position_embeddings), True if enable_pdl is None else bool(enable_pdl))
 
 
 # ------------------------------------------------------------------------------------------------
 # Paged KV cache append (alone, and fused with rope).
 # ------------------------------------------------------------------------------------------------
 @torch.library.register_fake("mas_b200::append_paged_kv_cache")
-def _(k, v, batch_indices, positions, k_cache, v_cache, kv_indices, kv_indptr, hnd, enable_pdl, status) -> None:
+def _(k, v, batch_indices, positions, k_cache, v_cache, kv_indices, kv_indptr, hnd, enable_pdl) -> None:
     return None
 
 
 @torch.library.register_fake("mas_b200::rope_append_paged_kv_cache")
 def _(q, k, v, cos_sin_cache, pos_ids, batch_indices, k_cache, v_cache, kv_indices, kv_indptr, interleave, hnd,
-      beta, original_max, enable_pdl, status) -> None:
+      beta, original_max, enable_pdl) -> None:
     return None
 
 
@@ -433,7 +407,7 @@ def append_paged_kv_cache(append_key: torch.Tensor, append_value: torch.Tensor, 
         return
     _OP_APPEND(append_key, append_value, _int32(batch_indices), positions.contiguous(), k_cache, v_cache,
                _int32(kv_indices), _int32(kv_indptr), kv_layout == "HND",
-               True if enable_pdl is None else bool(enable_pdl), _status_arg(append_key.device))
+               True if enable_pdl is None else bool(enable_pdl))
 
 
 def apply_rope_and_append_paged_kv_cache(positions: torch.Tensor, query: torch.Tensor, key: torch.Tensor,
@@ -480,19 +454,19 @@ def apply_rope_and_append_paged_kv_cache(positions: torch.Tensor, query: torch.T
     _OP_ROPE_APPEND(q, k, v, cos_sin_cache, positions.contiguous(), _int32(batch_indices), k_cache, v_cache,
                     _int32(kv_indices), _int32(kv_indptr), not is_neox, kv_layout == "HND",
                     float(llama_4_scaling_beta or 0.0), int(original_max_position_embeddings),
-                    True if enable_pdl is None else bool(enable_pdl), _status_arg(query.device))
+                    True if enable_pdl is None else bool(enable_pdl))
 
 
 # ------------------------------------------------------------------------------------------------
 # Token-embedding gather.
 # ------------------------------------------------------------------------------------------------
 @torch.library.register_fake("mas_b200::embedding")
-def _(input_ids, weight, enable_pdl, status):
+def _(input_ids, weight, enable_pdl):
     return weight.new_empty(tuple(input_ids.shape) + (weight.shape[1],))
 
 
 @torch.library.register_fake("mas_b200::embedding_out")
-def _(out, input_ids, weight, enable_pdl, status) -> None:
+def _(out, input_ids, weight, enable_pdl) -> None:
     return None
 
 
@@ -511,7 +485,7 @@ def embedding(input_ids: torch.Tensor, weight: torch.Tensor, enable_pdl: Optiona
     in the device status word (`read_status`), where aten would raise a device-side assert.
     """
     _check_embedding(input_ids, weight)
-    return _OP_EMBED(input_ids, weight, True if enable_pdl is None else bool(enable_pdl), _status_arg(weight.device))
+    return _OP_EMBED(input_ids, weight, True if enable_pdl is None else bool(enable_pdl))
 
 
 def embedding_out(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tensor,
@@ -523,13 +497,12 @@ def embedding_out(out: torch.Tensor, input_ids: torch.Tensor, weight: torch.Tens
     if not out.is_contiguous():
         raise ValueError("out must be contiguous")
     _check_device(weight, out=out)
-    _OP_EMBED_OUT(out, input_ids.contiguous(), weight, True if enable_pdl is None else bool(enable_pdl),
-                  _status_arg(weight.device))
+    _OP_EMBED_OUT(out, input_ids.contiguous(), weight, True if enable_pdl is None else bool(enable_pdl))
     return out
 
 
 @torch.library.register_fake("mas_b200::embedding_fill")
-def _(input_ids, weight, last_tokens, enable_pdl, status):
+def _(input_ids, weight, last_tokens, enable_pdl):
     return weight.new_empty(tuple(input_ids.shape) + (weight.shape[1],))
 
 
@@ -554,4 +527,4 @@ def embedding_fill_placeholders(input_ids: torch.Tensor, weight: torch.Tensor, l
     if not input_ids.is_contiguous():
         raise ValueError("input_ids must be contiguous (it is updated in place)")
     return _OP_EMBED_FILL(input_ids, weight, last_tokens.contiguous(),
-                          True if enable_pdl is None else bool(enable_pdl), _status_arg(weight.device))
+                          True if enable_pdl is None else bool(enable_pdl))

@@ -52,3 +52,62 @@ def test_measured_peak_source(tmp_path, monkeypatch):
     assert bench.measured_peak() == (bench.FALLBACK_HBM_GBS, "fallback")
     (tmp_path / "MEASURED_PEAKS.json").write_text(json.dumps({"hbm_gbs": 6500.5}))
     assert bench.measured_peak() == (6500.5, "measured")
+
+
+def _oracle_sample(quant: bool, layers: int = 2, n: int = 2) -> dict:
+    """A sample in the layout of ChainWorkload.sample_step, its outputs made by the oracle itself."""
+    import torch
+
+    import oracle
+    from mas_b200 import workloads as wl
+
+    s = wl.CHAIN_SHAPE
+    g = torch.Generator().manual_seed(11)
+    bf = torch.bfloat16
+    inp = {"ids": torch.tensor([3, 9]), "table_rows": (torch.randn(n, s.hidden_size, generator=g) * 0.02).to(bf),
+           "attn_out": torch.randn(n, s.hidden_size, generator=g).to(bf),
+           "qkv": torch.randn(n, s.qkv_size, generator=g).to(bf),
+           "gate_up": torch.randn(n, 2 * s.intermediate_size, generator=g).to(bf),
+           "cache_rows": torch.rand(n, s.head_dim, generator=g),
+           "w_in": (1 + 0.1 * torch.randn(layers, s.hidden_size, generator=g)).to(bf),
+           "w_post": (1 + 0.1 * torch.randn(layers, s.hidden_size, generator=g)).to(bf),
+           "act_scale": torch.tensor([0.05, 0.05, 0.0137])}
+    hidden, residual = inp["table_rows"].clone(), torch.zeros(n, s.hidden_size, dtype=bf)
+    attn, qkv = inp["attn_out"].clone(), inp["qkv"].clone()
+    act = torch.empty(n, s.intermediate_size, dtype=bf)
+    x8 = torch.empty(n, s.hidden_size, dtype=torch.float8_e4m3fn)
+    act8 = torch.empty(n, s.intermediate_size, dtype=torch.float8_e4m3fn)
+    pos = torch.arange(n, dtype=torch.int32)
+    for l in range(layers):
+        if quant:
+            oracle.fused_add_rmsnorm_quant(x8, hidden, residual, inp["w_in"][l], 0.05, s.rms_norm_eps)
+        else:
+            oracle.fused_add_rmsnorm(hidden, residual, inp["w_in"][l], s.rms_norm_eps)
+        oracle.apply_rope_with_cos_sin_cache_inplace(pos, qkv[:, : s.q_size], qkv[:, s.q_size: s.q_size + s.kv_size],
+                                                     s.head_dim, inp["cache_rows"])
+        if quant:
+            oracle.fused_add_rmsnorm_quant(x8, attn, residual, inp["w_post"][l], 0.05, s.rms_norm_eps)
+            oracle.silu_and_mul_quant(inp["gate_up"], float(inp["act_scale"][2]), out=act8)
+        else:
+            oracle.fused_add_rmsnorm(attn, residual, inp["w_post"][l], s.rms_norm_eps)
+            oracle.silu_and_mul(inp["gate_up"], out=act)
+    out = {"residual": residual, "qkv": qkv}
+    out.update({"x_fp8": x8, "act_fp8": act8} if quant else {"hidden": hidden, "attn_out": attn, "act": act})
+    return {"tokens": torch.arange(n), "quant": quant, "layers": layers, "inputs": inp, "outputs": out}
+
+
+@pytest.mark.parametrize("quant", [False, True])
+def test_oracle_check_of_sampled_rows(quant):
+    """bench.oracle_check replays a gathered sample through the oracle: zero distance for the oracle's
+    own outputs, and a planted one-step error in one output element is reported as exactly that."""
+    import torch
+
+    sample = _oracle_sample(quant)
+    got = bench.oracle_check(sample, 1e-5)
+    assert set(got) == set(sample["outputs"]) and max(got.values()) == 0, got
+    name = "x_fp8" if quant else "act"
+    t = sample["outputs"][name]
+    bits = t.view(torch.uint8 if quant else torch.int16)
+    bits[1, 5] += 1
+    got = bench.oracle_check(sample, 1e-5)
+    assert got[name] == 1 and max(v for k, v in got.items() if k != name) == 0, got

@@ -30,7 +30,7 @@ def test_header_declares_the_expected_entry_points():
     fns = declared_functions()
     for name in ("mas_fused_add_rmsnorm", "mas_fused_add_rmsnorm_quant", "mas_silu_and_mul",
                  "mas_rope_cos_sin_cache_inplace", "mas_embedding_gather", "mas_prepare_device",
-                 "mas_status_string", "mas_version", "mas_read_fault_word"):
+                 "mas_status_string", "mas_version", "mas_read_fault_word", "mas_read_status_word"):
         assert name in fns, name
 
 

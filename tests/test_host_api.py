@@ -87,9 +87,13 @@ def test_ops_registered_with_mutation_annotations():
         "fused_add_rmsnorm": ("input", "residual"),
         "fused_add_rmsnorm_quant": ("out", "residual"),
         "silu_and_mul": ("out",),
-        "apply_rope_pos_ids_cos_sin_cache": ("q", "k", "status"),
-        "embedding_out": ("out", "status"),
-        "embedding": ("status",),
+        "apply_rope_pos_ids_cos_sin_cache": ("q", "k"),
+        "apply_rope_q_scale": ("q", "k"),
+        "append_paged_kv_cache": ("k_cache", "v_cache"),
+        "rope_append_paged_kv_cache": ("q", "k", "k_cache", "v_cache"),
+        "embedding_out": ("out",),
+        "embedding": (),
+        "embedding_fill": ("input_ids",),
     }
     for name, mutated in expect.items():
         schema = getattr(torch.ops.mas_b200, name).default._schema
