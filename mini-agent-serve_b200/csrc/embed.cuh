@@ -4,7 +4,8 @@
 // miniagentserve/models/devstral2/devstral2.py:260, :282).
 //
 // Fast path (rows of a multiple of 16 bytes, 16-byte aligned): the TMA engine does the whole copy.
-// Each CTA is one warp that owns a contiguous block of output rows; it stages their ids in shared
+// Each CTA is one warp that owns a contiguous block of output rows (and, when a step has too few
+// rows to occupy every SM, one column chunk of them: blockIdx.y); it stages their ids in shared
 // memory (one coalesced read), then lane 0 keeps an S-stage ring busy: a bulk load of the table row
 // into a stage (mbarrier transaction count), then a bulk store of that stage into the output row
 // (bulk async-group), refilling a stage as soon as its store has finished reading it. Several
@@ -27,6 +28,8 @@ struct EmbedArgs {
   int64_t out_stride_b;    // bytes
   int64_t table_stride_b;  // bytes
   uint32_t row_bytes;
+  uint32_t chunk_bytes;    // fast path: bytes of a row one CTA copies (a multiple of 16; blockIdx.y picks
+                           // the chunk), the whole row unless few rows must be spread over the SMs
   int32_t stages;
   int32_t rows_per_cta;
   int32_t* status;
@@ -65,9 +68,10 @@ template <typename IdT>
 __global__ void __launch_bounds__(32) embed_tma_kernel(const EmbedArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int S = a.stages;
-  const uint32_t rb = a.row_bytes;
+  const uint32_t col0 = blockIdx.y * a.chunk_bytes;
+  const uint32_t rb = min(a.chunk_bytes, a.row_bytes - col0);
   unsigned char* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * rb);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)S * a.chunk_bytes);
   int64_t* sid = reinterpret_cast<int64_t*>(bars + S);
   const int lane = threadIdx.x;
 
@@ -88,15 +92,15 @@ __global__ void __launch_bounds__(32) embed_tma_kernel(const EmbedArgs a) {
   }
   __syncwarp();
 
-  const unsigned char* table = static_cast<const unsigned char*>(a.table);
-  unsigned char* out = static_cast<unsigned char*>(a.out);
+  const unsigned char* table = static_cast<const unsigned char*>(a.table) + col0;
+  unsigned char* out = static_cast<unsigned char*>(a.out) + col0;
   // Rows with an invalid id complete their stage without a copy (plain arrive).
   auto issue = [&](int k) {
     const int s = k % S;
     const int64_t id = sid[k];
     if (id >= 0) {
       mbar_arrive_expect_tx(&bars[s], rb);
-      bulk_load(ring + (size_t)s * rb, table + id * a.table_stride_b, rb, &bars[s]);
+      bulk_load(ring + (size_t)s * a.chunk_bytes, table + id * a.table_stride_b, rb, &bars[s]);
     } else {
       mbar_arrive(&bars[s]);
     }
@@ -115,7 +119,7 @@ __global__ void __launch_bounds__(32) embed_tma_kernel(const EmbedArgs a) {
     if (!ok) break;
     unsigned char* dst = out + (row0 + k) * a.out_stride_b;
     if (sid[k] >= 0) {
-      if (lane == 0) bulk_store(dst, ring + (size_t)s * rb, rb);
+      if (lane == 0) bulk_store(dst, ring + (size_t)s * a.chunk_bytes, rb);
     } else {
       for (uint32_t b = (uint32_t)lane * 16u; b < rb; b += kWarp * 16u)
         st_plain(dst + b, Vec16{0u, 0u, 0u, 0u});

@@ -283,10 +283,15 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
     }
   }
   if (fast_ok && H % 8 == 0 && !use_ring) {
-    // Row-block CTAs: threads per row grow with H (32 ... 256), 128 or 256 threads per CTA.
+    // Row-block CTAs: threads per row grow with H (32 ... 256), 128 or 256 threads per CTA. A step
+    // with few rows (at most about one or three per SM) has too few CTAs to hide a row's latency, so
+    // its rows get four or two times the threads (at H = 12288 in a CUDA graph: 64 rows 3.7 -> 2.8 us,
+    // 256 rows 4.8 -> 4.3 us; from 512 rows up the base count is best).
     static const int env_tpr = env_int("MAS_NORM_TPR", 0);
     static const int env_cta = env_int("MAS_NORM_CTA_THREADS", 0);
     int tpr = H <= 3072 ? 32 : H <= 6144 ? 64 : H <= 16384 ? 128 : 256;
+    if (a.rows <= (int64_t)st.sm_count) tpr *= 4;
+    else if (a.rows <= 3 * (int64_t)st.sm_count) tpr *= 2;
     if (env_tpr > 0) tpr = env_tpr;
     int cta = env_cta > 0 ? env_cta : std::max(128, tpr);
     tpr = std::max(32, std::min(tpr, kNormRowMaxThreads)) / 32 * 32;
@@ -721,9 +726,17 @@ static int rope_main(const void* positions, int positions_dtype, void* query, vo
     return neox ? launch(KERNEL<__half, int32_t, true>, GRID, blk, 0, stream, enable_pdl, a)        \
                 : launch(KERNEL<__half, int32_t, false>, GRID, blk, 0, stream, enable_pdl, a);      \
   } while (0)
-  // Token-staged TMA ring: q heads and k heads contiguous within each token, 16-byte aligned rows.
+  // Token-staged TMA ring: q heads and k heads contiguous within each token, 16-byte aligned rows,
+  // and enough tokens for the ring's prologue to pay off; a step with only a few tokens per SM goes to
+  // the vector kernel, which issues all its loads at once (in a CUDA graph at the chain's shape: 64
+  // tokens 2.8 -> 2.2 us, 256 tokens 3.6 -> 3.2 us; at 4352 tokens the ring takes 40 us, the vector
+  // kernel 44). The fused paged append always takes the ring.
   static const bool force_vec = env_is("MAS_ROPE_IMPL", "vec");
-  const bool ring = vec && !force_vec && head_size % 8 == 0 &&
+  static const bool force_ring = env_is("MAS_ROPE_IMPL", "ring");
+  static const int env_ring_min = env_int("MAS_ROPE_RING_MIN_TOKENS", 0);
+  const int64_t ring_min = env_ring_min > 0 ? env_ring_min : 4 * (int64_t)st->sm_count;
+  const bool few_tokens = app == nullptr && !force_ring && num_tokens < ring_min;
+  const bool ring = vec && !force_vec && !few_tokens && head_size % 8 == 0 &&
                     (num_q_heads == 0 || q_stride_head == head_size) &&
                     (num_kv_heads == 0 || k_stride_head == head_size);
   if (ring && (!app || append_ring_ok(*app, head_size))) {
@@ -889,20 +902,29 @@ static int gather_impl(void* out, const void* table, const void* ids, int ids_dt
   const bool tma = row_bytes % 16 == 0 && row_bytes <= 64 * 1024 && aligned(out, 16) &&
                    aligned(table, 16) && a.out_stride_b % 16 == 0 && a.table_stride_b % 16 == 0;
   if (tma) {
+    // Column chunks when the step has fewer rows than about four per SM: a row's copy is split over
+    // several CTAs (at least 2 KB each) so that every SM has copies in flight. Not with placeholder
+    // filling, whose id write-back one CTA per row must own.
+    static const int env_chunks = env_int("MAS_EMBED_CHUNKS", 0);
+    int64_t chunks = env_chunks > 0 ? env_chunks : ceil_div(4 * (int64_t)st->sm_count, num_tokens);
+    chunks = last != nullptr ? 1 : std::max<int64_t>(1, std::min<int64_t>(chunks, row_bytes / 2048));
+    a.chunk_bytes = (uint32_t)(ceil_div(ceil_div(row_bytes, chunks), 16) * 16);
+    chunks = ceil_div(row_bytes, a.chunk_bytes);
     static const int env_stages = env_int("MAS_EMBED_STAGES", 0);
-    int stages = env_stages > 0 ? env_stages : (int)std::max<int64_t>(2, std::min<int64_t>(8, (48 * 1024) / row_bytes));
+    int stages = env_stages > 0 ? env_stages : (int)std::max<int64_t>(2, std::min<int64_t>(8, (48 * 1024) / a.chunk_bytes));
     stages = std::max(2, std::min(16, stages));
-    const size_t ring = (size_t)stages * (size_t)row_bytes + 8 * (size_t)kEmbedMaxRowsPerCta;
+    const size_t ring = (size_t)stages * (size_t)a.chunk_bytes + 8 * (size_t)kEmbedMaxRowsPerCta;
     const int ctas = (int)std::max<size_t>(1, std::min<size_t>(16, kRingBytesPerSm / ring));
     int64_t grid = std::max<int64_t>((int64_t)st->sm_count * ctas, ceil_div(num_tokens, kEmbedMaxRowsPerCta));
     grid = std::min<int64_t>(grid, num_tokens);
     a.rows_per_cta = (int32_t)ceil_div(num_tokens, grid);
     grid = ceil_div(num_tokens, a.rows_per_cta);
     a.stages = stages;
-    const size_t smem = embed_tma_smem_bytes(a.row_bytes, stages, a.rows_per_cta);
-    if (smem <= kMaxSmemPerCta && grid <= INT32_MAX) {
-      if (i64) return launch(embed_tma_kernel<int64_t>, dim3((unsigned)grid), dim3(32), smem, stream, enable_pdl, a);
-      return launch(embed_tma_kernel<int32_t>, dim3((unsigned)grid), dim3(32), smem, stream, enable_pdl, a);
+    const size_t smem = embed_tma_smem_bytes(a.chunk_bytes, stages, a.rows_per_cta);
+    if (smem <= kMaxSmemPerCta && grid <= INT32_MAX && chunks <= 65535) {
+      const dim3 g((unsigned)grid, (unsigned)chunks);
+      if (i64) return launch(embed_tma_kernel<int64_t>, g, dim3(32), smem, stream, enable_pdl, a);
+      return launch(embed_tma_kernel<int32_t>, g, dim3(32), smem, stream, enable_pdl, a);
     }
   }
   int unit = 16;

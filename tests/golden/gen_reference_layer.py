@@ -2,6 +2,9 @@
 
     PYTHONPATH=<mini-agent-serve checkout> python tests/golden/gen_reference_layer.py
 
+(The reference's quantize_fp8 is torch.compile'd; on the CPU that needs a C++ compiler with OpenMP,
+chosen through the CXX environment variable.)
+
 The reference's model (miniagentserve/models/devstral2/devstral2.py:255-308, decoder layer :230-253,
 attention :139-210, MLP :213-224) is built at small dimensions with seeded random weights and run
 once, eagerly, on the CPU over a mixed step (decode rows, then prompt chunks) with a paged KV cache.
@@ -56,7 +59,6 @@ class Log:
     def call(self, name: str, fn, args: tuple, kwargs: dict):
         """Logs one call of `fn(*args, **kwargs)`: tensor layouts and storages before/after."""
         storages: dict[int, dict] = {}
-        desc = []
 
         def describe(v):
             if isinstance(v, torch.Tensor):
@@ -111,7 +113,7 @@ def _append(append_key, append_value, batch_indices, positions, paged_kv_cache, 
                                         kv_indices, kv_indptr, kv_layout) == 0
 
 
-def _attention_standin(*, query, out, **_):
+def _pass_query_through(query, out):
     out.copy_(query)
 
 
@@ -121,12 +123,20 @@ def logged(name, fn):
     return wrapper
 
 
+def logged_attention(name):
+    """The attention stand-in: logs the query the forward hands over (its layout and values) and the
+    output slice, and ignores the cache, workspace and lengths (not part of this path)."""
+    def wrapper(*, query, out, **_):
+        return LOG.call(name, _pass_query_through, (), {"query": query, "out": out})
+    return wrapper
+
+
 def config() -> Devstral2Config:
     return Devstral2Config(
         vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
         num_key_value_heads=2, head_dim=128, rms_norm_eps=1e-5, max_position_embeddings=1024, bos_token_id=1,
         eos_token_id=2, pad_token_id=11, rope_theta=1e6, dtype=torch.bfloat16, rope_factor=4.0,
-        rope_original_max_position_embeddings=256, rope_beta_fast=32.0, rope_beta_slow=1.0, rope_mscale=1.0,
+        rope_original_max_position_embeddings=16, rope_beta_fast=32.0, rope_beta_slow=1.0, rope_mscale=1.0,
         rope_mscale_all_dim=1.0, rope_truncate=True, llama_4_scaling_beta=0.1)
 
 
@@ -143,7 +153,12 @@ def build_model(cfg: Devstral2Config, g: torch.Generator) -> ref.Devstral2Model:
                 lin.weight_scale_inv.fill_(1.0 / (16 * lin.weight.shape[1] ** 0.5))
                 lin.activation_scale.fill_(0.02)
         model.norm.copy_(1 + 0.1 * torch.randn(cfg.hidden_size, generator=g))
-    return model.to(torch.bfloat16).eval()
+    # As from_pretrained leaves it (devstral2.py:330-345): embedding and norm weights in the model
+    # dtype; fp8 weights, fp32 scales and the fp32 cos/sin cache untouched.
+    for p in [model.embed_tokens.weight, model.norm] + [w for l in model.layers
+                                                        for w in (l.input_layernorm, l.post_attention_layernorm)]:
+        p.data = p.data.to(cfg.dtype)
+    return model.eval()
 
 
 def step_inputs(cfg: Devstral2Config, g: torch.Generator, block: int = 16):
@@ -186,8 +201,8 @@ def main() -> None:
     ref.apply_rope_with_cos_sin_cache_inplace = logged("apply_rope_with_cos_sin_cache_inplace", _rope)
     ref.append_paged_kv_cache = logged("append_paged_kv_cache", _append)
     ref.quantize_fp8 = logged("quantize_fp8", ref.quantize_fp8)
-    ref.trtllm_batch_decode_with_kv_cache = logged("attention_decode", _attention_standin)
-    ref.trtllm_batch_context_with_kv_cache = logged("attention_prefill", _attention_standin)
+    ref.trtllm_batch_decode_with_kv_cache = logged_attention("attention_decode")
+    ref.trtllm_batch_context_with_kv_cache = logged_attention("attention_prefill")
     embed_forward = model.embed_tokens.forward
     model.embed_tokens.forward = lambda ids: LOG.call("embedding", embed_forward, (ids,), {})
 
