@@ -3,7 +3,8 @@
 // Replaces the aten/inductor embedding behind nn.Embedding (Devstral2Model.embed_tokens,
 // miniagentserve/models/devstral2/devstral2.py:260, :282).
 //
-// Fast path (rows of a multiple of 16 bytes, 16-byte aligned): the TMA engine does the whole copy.
+// TMA path (rows of a multiple of 16 bytes, 16-byte aligned; placeholder filling, or on request):
+// the TMA engine does the whole copy.
 // Each CTA is one warp that owns a contiguous block of output rows (and, when a step has too few
 // rows to occupy every SM, one column chunk of them: blockIdx.y); it stages their ids in shared
 // memory (one coalesced read), then lane 0 keeps an S-stage ring busy: a bulk load of the table row
@@ -145,6 +146,42 @@ __global__ void __launch_bounds__(32) embed_tma_kernel(const EmbedArgs a) {
     bulk_wait_all();  // the ring must not be released while a store still reads it
   }
   __syncwarp();
+  pdl_launch_dependents();
+}
+
+// Register path (the default for aligned rows): CTA (row, column block) copies its block of the row
+// (blocks of equal size, chunk_bytes each, at most kEmbedVecPerThread 16-byte vectors per thread),
+// every load issued before any store, so a row costs about one HBM round trip instead of a bulk load
+// followed by a bulk store.
+// (Not used with placeholder filling: the CTAs of one row would race on the id write-back.)
+constexpr int kEmbedVecThreads = 128;
+constexpr int kEmbedVecPerThread = 4;
+
+template <typename IdT>
+__global__ void __launch_bounds__(kEmbedVecThreads) embed_vec_kernel(const EmbedArgs a) {
+  pdl_wait();
+  const int64_t t = blockIdx.x;
+  const int64_t id = (int64_t)static_cast<const IdT*>(a.ids)[t];
+  const bool valid = id >= 0 && id < a.V;
+  if (!valid && blockIdx.y == 0 && threadIdx.x == 0) flag_status(a.status, MAS_STATUS_EMBED_ID_OUT_OF_RANGE);
+  // column block blockIdx.y: vectors [b0, b1) of the row, blocks of equal size (chunk_bytes / 16)
+  const uint32_t nvec = a.row_bytes >> 4;
+  const uint32_t b0 = blockIdx.y * (a.chunk_bytes >> 4);
+  const uint32_t b1 = min(nvec, b0 + (a.chunk_bytes >> 4));
+  const uint32_t v0 = b0 + threadIdx.x;
+  const unsigned char* src = static_cast<const unsigned char*>(a.table) + (valid ? id : 0) * a.table_stride_b;
+  unsigned char* dst = static_cast<unsigned char*>(a.out) + t * a.out_stride_b;
+  Vec16 v[kEmbedVecPerThread];
+#pragma unroll
+  for (int j = 0; j < kEmbedVecPerThread; ++j) {
+    const uint32_t u = v0 + (uint32_t)j * kEmbedVecThreads;
+    if (u < b1) v[j] = valid ? ld_stream(src + (size_t)u * 16) : Vec16{0u, 0u, 0u, 0u};
+  }
+#pragma unroll
+  for (int j = 0; j < kEmbedVecPerThread; ++j) {
+    const uint32_t u = v0 + (uint32_t)j * kEmbedVecThreads;
+    if (u < b1) st_plain(dst + (size_t)u * 16, v[j]);
+  }
   pdl_launch_dependents();
 }
 

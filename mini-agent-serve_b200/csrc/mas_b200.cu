@@ -729,12 +729,12 @@ static int rope_main(const void* positions, int positions_dtype, void* query, vo
   // Token-staged TMA ring: q heads and k heads contiguous within each token, 16-byte aligned rows,
   // and enough tokens for the ring's prologue to pay off; a step with only a few tokens per SM goes to
   // the vector kernel, which issues all its loads at once (in a CUDA graph at the chain's shape: 64
-  // tokens 2.8 -> 2.2 us, 256 tokens 3.6 -> 3.2 us; at 4352 tokens the ring takes 40 us, the vector
-  // kernel 44). The fused paged append always takes the ring.
+  // tokens 2.8 -> 2.2 us, 256 tokens 3.6 -> 3.2 us; from 512 tokens the ring is faster: 5.1 against
+  // 5.7 us, and 40 against 44 us at 4352). The fused paged append always takes the ring.
   static const bool force_vec = env_is("MAS_ROPE_IMPL", "vec");
   static const bool force_ring = env_is("MAS_ROPE_IMPL", "ring");
   static const int env_ring_min = env_int("MAS_ROPE_RING_MIN_TOKENS", 0);
-  const int64_t ring_min = env_ring_min > 0 ? env_ring_min : 4 * (int64_t)st->sm_count;
+  const int64_t ring_min = env_ring_min > 0 ? env_ring_min : 2 * (int64_t)st->sm_count;
   const bool few_tokens = app == nullptr && !force_ring && num_tokens < ring_min;
   const bool ring = vec && !force_vec && !few_tokens && head_size % 8 == 0 &&
                     (num_q_heads == 0 || q_stride_head == head_size) &&
@@ -901,12 +901,27 @@ static int gather_impl(void* out, const void* table, const void* ids, int ids_dt
   const bool i64 = ids_dtype == MAS_DTYPE_INT64;
   const bool tma = row_bytes % 16 == 0 && row_bytes <= 64 * 1024 && aligned(out, 16) &&
                    aligned(table, 16) && a.out_stride_b % 16 == 0 && a.table_stride_b % 16 == 0;
+  // The register path, one CTA per row and column block of 8 KB, all loads before the stores. In a
+  // CUDA graph at H = 12288 it beat the TMA ring at every step size measured: 1.43 against 2.17 us
+  // at 64 rows, 5.58 against 6.78 us at 1024, 34.8 against 36.1 us at 4352. The ring stays for
+  // placeholder filling (one CTA per row must own the id write-back) and on request.
+  static const bool force_tma = env_is("MAS_EMBED_IMPL", "tma");
+  if (tma && last == nullptr && !force_tma) {
+    const int64_t nvec = row_bytes / 16;
+    const int64_t blocks = ceil_div(nvec, (int64_t)kEmbedVecThreads * kEmbedVecPerThread);
+    a.chunk_bytes = (uint32_t)(ceil_div(nvec, blocks) * 16);  // equal blocks: 10 KB rows -> 2 x 5 KB
+    const dim3 g((unsigned)std::min<int64_t>(num_tokens, INT32_MAX), (unsigned)blocks);
+    if (num_tokens <= INT32_MAX) {
+      if (i64) return launch(embed_vec_kernel<int64_t>, g, dim3(kEmbedVecThreads), 0, stream, enable_pdl, a);
+      return launch(embed_vec_kernel<int32_t>, g, dim3(kEmbedVecThreads), 0, stream, enable_pdl, a);
+    }
+  }
   if (tma) {
-    // Column chunks when the step has fewer rows than about four per SM: a row's copy is split over
-    // several CTAs (at least 2 KB each) so that every SM has copies in flight. Not with placeholder
-    // filling, whose id write-back one CTA per row must own.
+    // Optional column chunks (MAS_EMBED_CHUNKS): a row's copy split over several CTAs. Measured no
+    // better than whole rows at 64-1024 rows (the register path above serves small steps); off by
+    // default. Never with placeholder filling, whose id write-back one CTA per row must own.
     static const int env_chunks = env_int("MAS_EMBED_CHUNKS", 0);
-    int64_t chunks = env_chunks > 0 ? env_chunks : ceil_div(4 * (int64_t)st->sm_count, num_tokens);
+    int64_t chunks = env_chunks > 0 ? env_chunks : 1;
     chunks = last != nullptr ? 1 : std::max<int64_t>(1, std::min<int64_t>(chunks, row_bytes / 2048));
     a.chunk_bytes = (uint32_t)(ceil_div(ceil_div(row_bytes, chunks), 16) * 16);
     chunks = ceil_div(row_bytes, a.chunk_bytes);
