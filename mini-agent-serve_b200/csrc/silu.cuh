@@ -170,8 +170,11 @@ __device__ __forceinline__ QuantDiv make_quant_div(float s) {
 // pair takes the remainder-corrected quotient. Checked on the CPU over every bf16 and fp16 input.
 __device__ __forceinline__ uint16_t quant2_e4m3(float x0, float x1, const QuantDiv& div) {
   if (div.fast) {
-    const uint16_t lo = f2_to_e4m3x2(__fmul_rn(x0, div.r_lo), __fmul_rn(x1, div.r_lo));
-    const uint16_t hi = f2_to_e4m3x2(__fmul_rn(x0, div.r_hi), __fmul_rn(x1, div.r_hi));
+    const float2 x = make_float2(x0, x1);
+    const float2 lo2 = mul2_f32(x, make_float2(div.r_lo, div.r_lo));
+    const float2 hi2 = mul2_f32(x, make_float2(div.r_hi, div.r_hi));
+    const uint16_t lo = f2_to_e4m3x2(lo2.x, lo2.y);
+    const uint16_t hi = f2_to_e4m3x2(hi2.x, hi2.y);
     if (lo == hi) return lo;
   }
   return f2_to_e4m3x2(div(x0), div(x1));
@@ -179,6 +182,18 @@ __device__ __forceinline__ uint16_t quant2_e4m3(float x0, float x1, const QuantD
 
 __device__ __forceinline__ uint32_t quant4_e4m3(const float* act, const QuantDiv& div) {
   return (uint32_t)quant2_e4m3(act[0], act[1], div) | ((uint32_t)quant2_e4m3(act[2], act[3], div) << 16);
+}
+
+// quant4_e4m3 for a scale whose reciprocal is a normal number (div.fast): the four codes of both
+// brackets are compared at once; only when they differ does each pair take quant2_e4m3's path.
+__device__ __forceinline__ uint32_t quant4_e4m3_fast(const float* act, const QuantDiv& div) {
+  const float2 rl = make_float2(div.r_lo, div.r_lo), rh = make_float2(div.r_hi, div.r_hi);
+  const float2 l01 = mul2_f32(make_float2(act[0], act[1]), rl), l23 = mul2_f32(make_float2(act[2], act[3]), rl);
+  const float2 h01 = mul2_f32(make_float2(act[0], act[1]), rh), h23 = mul2_f32(make_float2(act[2], act[3]), rh);
+  const uint32_t lo = (uint32_t)f2_to_e4m3x2(l01.x, l01.y) | ((uint32_t)f2_to_e4m3x2(l23.x, l23.y) << 16);
+  const uint32_t hi = (uint32_t)f2_to_e4m3x2(h01.x, h01.y) | ((uint32_t)f2_to_e4m3x2(h23.x, h23.y) << 16);
+  if (lo == hi) return lo;
+  return quant4_e4m3(act, div);
 }
 
 // Register variant (the default fast path): one 16-byte gate/up pair per thread and row, 32
@@ -207,12 +222,21 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
       unpack8<T>(gv, gf);
       unpack8<T>(uv, uf);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = silu_f32(gf[e]) * uf[e];
+      for (int e = 0; e < 8; e += 2) {
+        const float2 p = mul2_f32(make_float2(silu_f32(gf[e]), silu_f32(gf[e + 1])), make_float2(uf[e], uf[e + 1]));
+        y[e] = p.x;
+        y[e + 1] = p.y;
+      }
       if constexpr (QUANT) {
         unpack8<T>(pack8<T>(y), y);  // the activation as the unfused op would have stored it
         uint2 q;
-        q.x = quant4_e4m3(y, div);
-        q.y = quant4_e4m3(y + 4, div);
+        if (div.fast) {
+          q.x = quant4_e4m3_fast(y, div);
+          q.y = quant4_e4m3_fast(y + 4, div);
+        } else {
+          q.x = quant4_e4m3(y, div);
+          q.y = quant4_e4m3(y + 4, div);
+        }
         *reinterpret_cast<uint2*>(static_cast<uint8_t*>(a.out) + row * a.out_stride + (size_t)v * 8) = q;
       } else {
         st_plain(static_cast<T*>(a.out) + row * a.out_stride + (size_t)v * 8, pack8<T>(y));
