@@ -109,6 +109,20 @@ __device__ __forceinline__ float2 mul2_f32(float2 a, float2 b) {
   return c;
 }
 
+// a * b + c on two fp32 pairs, one rounding per lane (two scalar fmas, one issue slot).
+__device__ __forceinline__ float2 fma2_f32(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Global memory access.
 // ---------------------------------------------------------------------------------------------

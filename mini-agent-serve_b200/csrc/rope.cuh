@@ -61,6 +61,22 @@ __device__ __forceinline__ void rotate(float a, float b, float c, float s, float
   rb = __fmaf_rn(b, c, __fmul_rn(a, s));
 }
 
+// `rotate` on the 8 neox pairs (x0[e], x1[e]) of one group, two pairs per packed instruction:
+// b*(-s) is exactly -(b*s), so with nsn = -sn the packed form rounds every lane as `rotate` does.
+__device__ __forceinline__ void rotate8_neox(const float (&x0)[8], const float (&x1)[8], const float (&cs)[8],
+                                             const float (&sn)[8], const float (&nsn)[8], float (&o0)[8],
+                                             float (&o1)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    const float2 a = make_float2(x0[e], x0[e + 1]), b = make_float2(x1[e], x1[e + 1]);
+    const float2 c = make_float2(cs[e], cs[e + 1]);
+    const float2 ra = fma2_f32(a, c, mul2_f32(b, make_float2(nsn[e], nsn[e + 1])));
+    const float2 rb = fma2_f32(b, c, mul2_f32(a, make_float2(sn[e], sn[e + 1])));
+    o0[e] = ra.x; o0[e + 1] = ra.y;
+    o1[e] = rb.x; o1[e + 1] = rb.y;
+  }
+}
+
 // llama-4 query scale of a token (Devstral2Attention.forward, devstral2.py:175-179), evaluated the
 // way eager torch evaluates `1 + beta * log1p(floor(pos.float() / original_max))` on CUDA: the
 // division by the host scalar is a multiplication by its fp32 reciprocal, every operation is rounded
@@ -330,7 +346,7 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
         const float qs = a.q_beta != 0.f ? llama4_q_scale<T>(spos[i], a.q_beta, a.q_inv_orig) : 0.f;
         const uint32_t qs2 = Elem<T>::from_f2(qs, qs);  // exact: qs is already a T value
         // One group: the 8 rotation pairs of staged head h held in the 16-byte vectors at off0, off1.
-        const auto group = [&](int h, int j, const float (&cs)[8], const float (&sn)[8]) {
+        const auto group = [&](int h, int j, const float (&cs)[8], const float (&sn)[8], const float (&nsn)[8]) {
           const T* sh = reinterpret_cast<const T*>(st) + (size_t)h * a.D;  // staged head (q then k)
           T* gh = h < a.Hq ? qb + t * a.qsn + (int64_t)h * a.D : kb + t * a.ksn + (int64_t)(h - a.Hq) * a.D;
           const int off0 = NEOX ? j * 8 : j * 16;
@@ -339,8 +355,7 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
           unpack8<T>(*reinterpret_cast<const Vec16*>(sh + off0), x0);
           unpack8<T>(*reinterpret_cast<const Vec16*>(sh + off1), x1);
           if constexpr (NEOX) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) rotate(x0[e], x1[e], cs[e], sn[e], o0[e], o1[e]);
+            rotate8_neox(x0, x1, cs, sn, nsn, o0, o1);
           } else {
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -363,7 +378,8 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
           }
         };
         // cos/sin of pair group j (cos in c[0, half), sin in c[half, rd)).
-        const auto load_cs = [&](int j, float (&cs)[8], float (&sn)[8]) {
+        // (nsn = -sn feeds the packed neox rotation.)
+        const auto load_cs = [&](int j, float (&cs)[8], float (&sn)[8], float (&nsn)[8]) {
           const float4 c0 = *reinterpret_cast<const float4*>(c + j * 8);
           const float4 c1 = *reinterpret_cast<const float4*>(c + j * 8 + 4);
           const float4 s0 = *reinterpret_cast<const float4*>(c + half + j * 8);
@@ -372,18 +388,20 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
           cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
           sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
           sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) nsn[e] = NEOX ? -sn[e] : 0.f;
         };
         if (fixed_j) {
-          float cs[8], sn[8];
-          load_cs(jf, cs, sn);
-          for (int h = h0; h < NH; h += hstep) group(h, jf, cs, sn);
+          float cs[8], sn[8], nsn[8];
+          load_cs(jf, cs, sn, nsn);
+          for (int h = h0; h < NH; h += hstep) group(h, jf, cs, sn, nsn);
         } else {
           for (int gi = ct; gi < groups; gi += ncons) {
             const int h = gi / tpu;
             const int j = gi - h * tpu;
-            float cs[8], sn[8];
-            load_cs(j, cs, sn);
-            group(h, j, cs, sn);
+            float cs[8], sn[8], nsn[8];
+            load_cs(j, cs, sn, nsn);
+            group(h, j, cs, sn, nsn);
           }
         }
         if constexpr (APPEND) {
