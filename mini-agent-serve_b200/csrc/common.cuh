@@ -216,6 +216,17 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// Before a ring kernel's CTA exits after a wait gave up: waits (bounded) for the latest phase of
+// every stage whose loads were issued, so no bulk copy is still writing into this CTA's shared
+// memory when it is released. `issued` loads went to stages k % stages in order, and a barrier's
+// phases complete in order, so the latest phase of each stage covers the earlier ones.
+__device__ __forceinline__ void drain_ring(uint64_t* full, int stages, int issued) {
+  for (int s = 0; s < stages && s < issued; ++s) {
+    const int k = s + ((issued - 1 - s) / stages) * stages;  // the last load into stage s
+    (void)mbar_wait_bounded(&full[s], (uint32_t)(k / stages) & 1u);
+  }
+}
+
 // Global -> shared bulk copy, completion counted on `bar` (bytes: multiple of 16, both addresses
 // 16-byte aligned). The destination is this CTA's own shared memory.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,

@@ -113,14 +113,18 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
   T* const xb = static_cast<T*>(a.x);
   T* const rb = static_cast<T*>(a.r);
 
+  int issued = 0;        // producer lane: rows whose copies were issued
+  bool gave_up = false;  // this thread's (or its group's) bounded wait ran out
   if (warp == 0) {
     if (lane == 0) {
       for (int k = 0; k < n; ++k) {
         const int s = k % S;
         if (k >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((k / S) - 1) & 1u)) {
           atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+          gave_up = true;
           break;
         }
+        issued = k + 1;
         unsigned char* st = ring + (size_t)s * 2 * row_bytes;
         mbar_arrive_expect_tx(&full[s], 2 * row_bytes);
         bulk_load(st, xb + (row0 + k) * a.x_stride, row_bytes, &full[s]);
@@ -184,6 +188,7 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
       if (lane == 0) red_k[cw] = ss;
       if (group_sync_or(1 + g, !ok, gsize)) {
         if (ct == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+        gave_up = true;
         break;
       }
       float tot = 0.f;
@@ -226,6 +231,9 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
       }
     }
   }
+  // After a wait gave up anywhere in the CTA, the producer lane waits for the copies it issued
+  // before the CTA's shared memory is released.
+  if (__syncthreads_or(gave_up) && tid == 0) drain_ring(full, S, issued);
   pdl_launch_dependents();
 }
 

@@ -299,14 +299,18 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
 
   T* const qb = static_cast<T*>(a.q);
   T* const kb = static_cast<T*>(a.k);
+  int issued = 0;     // producer lane: tokens whose stage has been filled (or marked empty)
+  bool gave_up = false;  // this thread's bounded wait ran out
   if (warp == 0) {
     if (lane == 0) {
       for (int i = 0; i < n; ++i) {
         const int s = i % S;
         if (i >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((i / S) - 1) & 1u)) {
           atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+          gave_up = true;
           break;
         }
+        issued = i + 1;
         const int64_t pos = spos[i];
         if (pos < 0) {
           mbar_arrive(&full[s]);
@@ -334,8 +338,10 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
     const int jf = ct % tpu, h0 = ct / tpu, hstep = ncons / tpu;
     for (int i = 0; i < n; ++i) {
       const int s = i % S;
-      if (!mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u)) {
+      // every lane waits (each needs the barrier's acquire); the warp gives up as one
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (uint32_t)(i / S) & 1u))) {
         if (lane == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+        gave_up = true;
         break;
       }
       if (spos[i] >= 0) {
@@ -435,6 +441,9 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
       if (lane == 0) mbar_arrive(&empty[s]);
     }
   }
+  // After a wait gave up anywhere in the CTA, the producer lane waits for the copies it issued
+  // before the CTA's shared memory is released.
+  if (__syncthreads_or(gave_up) && tid == 0) drain_ring(full, S, issued);
   pdl_launch_dependents();
 }
 

@@ -73,6 +73,8 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
   __syncthreads();
   pdl_wait();
 
+  int issued = 0;        // producer lane: tiles whose loads were issued
+  bool gave_up = false;  // this thread's bounded wait ran out
   if (warp == 0) {
     // Producer. A failed wait (which means a copy or a consumer never finished) ends the stream.
     if (lane == 0) {
@@ -81,8 +83,10 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
         const int s = k % S;
         if (k >= S && !mbar_wait_bounded(&empty[s], (uint32_t)((k / S) - 1) & 1u)) {
           atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+          gave_up = true;
           break;
         }
+        issued = k + 1;
         const int64_t tile = t0 + k;
         const int64_t row = tile / cpr;
         const int c0 = (int)(tile - row * cpr) * kSiluChunk;
@@ -99,8 +103,10 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
     T* out = static_cast<T*>(a.out);
     for (int k = 0; k < n; ++k) {
       const int s = k % S;
-      if (!mbar_wait_bounded(&full[s], (uint32_t)(k / S) & 1u)) {
+      // every lane waits (each needs the barrier's acquire); the warp gives up as one
+      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], (uint32_t)(k / S) & 1u))) {
         if (lane == 0) atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+        gave_up = true;
         break;
       }
       const int64_t tile = t0 + k;
@@ -122,6 +128,9 @@ __global__ void __launch_bounds__(kSiluRingThreads) silu_mul_ring_kernel(const S
       if (lane == 0) mbar_arrive(&empty[s]);
     }
   }
+  // After a wait gave up anywhere in the CTA, the producer lane waits for the copies it issued
+  // before the CTA's shared memory is released.
+  if (__syncthreads_or(gave_up) && tid == 0) drain_ring(full, S, issued);
   pdl_launch_dependents();
 }
 
