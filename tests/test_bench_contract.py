@@ -111,3 +111,13 @@ def test_oracle_check_of_sampled_rows(quant):
     bits[1, 5] += 1
     got = bench.oracle_check(sample, 1e-5)
     assert got[name] == 1 and max(v for k, v in got.items() if k != name) == 0, got
+
+
+@pytest.mark.parametrize("workload", sorted(bench.NCU_IN_CHAIN))
+def test_in_chain_time_is_backed_by_a_profile(workload):
+    """The dominant kernel's in-chain mean (roofline.ncu_in_chain_us) is the mean of a committed
+    ncu launch list of the bench's own command."""
+    us, source = bench.NCU_IN_CHAIN[workload]
+    text = (ROOT / source).read_text()
+    assert f"{us:.2f}" in text, (workload, us, source)
+    assert "gpu__time_duration.sum" in text and "--clock-control none" in text
