@@ -756,10 +756,13 @@ def host_cores() -> int:
 
 
 def calibrate_cpu_tokens(layers: int, target_s: float) -> int:
-    probe = CpuChainSample(16, layers)
+    """Tokens whose step takes about target_s on this host (the probe's first step, which pays for
+    thread start-up and first-touch page faults, is not used)."""
+    probe = CpuChainSample(64, layers)
+    probe.step()
     t0 = time.perf_counter()
     probe.step()
-    per_token = (time.perf_counter() - t0) / 16
+    per_token = (time.perf_counter() - t0) / 64
     return int(max(16, min(4352, target_s / max(per_token, 1e-9))))
 
 
@@ -1027,7 +1030,7 @@ def run_gpu_arm(args, dist: Dist) -> None:
 
         cores = host_cores()
         oracle.set_num_threads(cores)
-        tokens = calibrate_cpu_tokens(layers, 3.0)
+        tokens = calibrate_cpu_tokens(layers, 4.0)
         value_cpu, times = time_cpu_chain(tokens, layers, reps=3)
         cpu = {"value": value_cpu, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{tokens} of {w.tokens} tokens, all {layers} layers, median of 3 steps "
