@@ -121,3 +121,31 @@ def test_in_chain_time_is_backed_by_a_profile(workload):
     text = (ROOT / source).read_text()
     assert f"{us:.2f}" in text, (workload, us, source)
     assert "gpu__time_duration.sum" in text and "--clock-control none" in text
+
+
+def _maps_after(code: str) -> str:
+    """/proc/self/maps of a fresh interpreter after running `code` (the repo root on sys.path)."""
+    import subprocess
+    import sys
+
+    prog = f"import sys; sys.path.insert(0, {str(ROOT)!r})\n{code}\nprint(open('/proc/self/maps').read())"
+    r = subprocess.run([sys.executable, "-c", prog], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return r.stdout
+
+
+def test_host_modules_do_not_map_the_cuda_library():
+    maps = _maps_after("import mas_b200\nfrom mas_b200 import workloads, chain, rope_cache\n"
+                       "rope_cache.plain_cos_sin_cache(128, 64, 1e6)")
+    assert "libmas_b200" not in maps
+
+
+def test_reference_arm_maps_only_the_oracle():
+    """bench.py --impl reference times the reference's CPU path: the oracle and torch, nothing of
+    this repository's CUDA code."""
+    maps = _maps_after("import runpy, sys\n"
+                       "sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '3', '--layers', '1']\n"
+                       "runpy.run_path('bench.py', run_name='__main__')")
+    assert "libmas_b200" not in maps and "liborc" in maps
+    line = json.loads([l for l in maps.splitlines() if l.startswith("{")][-1])
+    assert line["impl"] == "reference" and line["config"] == bench.chain_config(1, 4352, 4352)
