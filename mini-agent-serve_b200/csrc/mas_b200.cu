@@ -82,6 +82,10 @@ cudaError_t opt_in_norm_row() {
   if (e == cudaSuccess) e = opt_in_smem(norm_loop_kernel<T, Q, 8>);
   if (e == cudaSuccess) e = opt_in_smem(norm_loop_kernel<T, Q, 12>);
   if (e == cudaSuccess) e = opt_in_smem(norm_loop_kernel<T, Q, 16>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 4>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 6>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 8>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 12>);
   return e;
 }
 
@@ -245,9 +249,10 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
   static const bool use_ring = env_is("MAS_NORM_IMPL", "ring");
   static const bool use_row = env_is("MAS_NORM_IMPL", "row");
   static const bool use_loop = env_is("MAS_NORM_IMPL", "loop");
+  static const bool use_rowreg = env_is("MAS_NORM_IMPL", "rowreg");
   // Default: the persistent loop up to H = 6144 (config 1's H = 5120 measured 26.3 us against 29.5
-  // for the row-block grid), the row-block grid above (H = 12288: 67 us against 73+ for the loop).
-  if (fast_ok && H % 8 == 0 && (use_loop || (!use_ring && !use_row && H <= 6144))) {
+  // for the row-block grid), the register-resident row kernel above (below).
+  if (fast_ok && H % 8 == 0 && (use_loop || (!use_ring && !use_row && !use_rowreg && H <= 6144))) {
     // Persistent row-group loop (norm_loop_kernel): S-stage ring, every thread a consumer. By
     // default at most 4 vectors per thread (threads per row = H/32, rounded up to a warp), CTAs of at
     // least 128 threads (one row each from 128 threads per row up) and two stages: at H = 5120, four
@@ -281,6 +286,20 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
       if (vpt <= 12) return launch(norm_loop_kernel<T, Q, 12>, g, b, smem, stream, pdl, a, tpr, rpc);
       return launch(norm_loop_kernel<T, Q, 16>, g, b, smem, stream, pdl, a, tpr, rpc);
     }
+  }
+  // Above H = 6144 (up to 12288) the register-resident row kernel, except for steps of at most one
+  // row per SM, where the row kernel with four times the threads per row is faster (2.9 against
+  // 3.0 us at 64 rows). At H = 12288: 4352 rows 65.6-65.7 us (row kernel 66.6-67.2, flashinfer
+  // 65.9-66.0), e4m3 out 57.5-57.6 us (60.0-60.3, flashinfer 70.1-70.8), 256 rows 4.0 us (4.3-4.5).
+  const bool rowreg_default = !use_ring && !use_row && !use_loop && H > 6144 && a.rows > (int64_t)st.sm_count;
+  if (fast_ok && H % 8 == 0 && (use_rowreg || rowreg_default) && H / 8 <= 12 * 128 && a.rows <= INT32_MAX) {
+    const int nv = H / 8;
+    const size_t smem = 2 * (size_t)H * sizeof(T) + 16 + 4 * sizeof(float);
+    const dim3 g((unsigned)a.rows), b(128);
+    if (nv <= 4 * 128) return launch(norm_row_keep_kernel<T, Q, 4>, g, b, smem, stream, pdl, a);
+    if (nv <= 6 * 128) return launch(norm_row_keep_kernel<T, Q, 6>, g, b, smem, stream, pdl, a);
+    if (nv <= 8 * 128) return launch(norm_row_keep_kernel<T, Q, 8>, g, b, smem, stream, pdl, a);
+    return launch(norm_row_keep_kernel<T, Q, 12>, g, b, smem, stream, pdl, a);
   }
   if (fast_ok && H % 8 == 0 && !use_ring) {
     // Row-block CTAs: threads per row grow with H (32 ... 256), 128 or 256 threads per CTA. A step

@@ -352,6 +352,99 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
   pdl_launch_dependents();
 }
 
+// Row-block variant that keeps h = x + r in registers between the two passes (one row of 128
+// threads per CTA, at most MAXV vectors per thread): the second pass needs no shared-memory re-read
+// and no re-unpacking, at the price of about 160 registers a thread at MAXV = 12 (3 CTAs per SM
+// instead of 4; the launch bounds hold the compiler to that, without them it took 178 registers and
+// fit only 2).
+template <typename T, bool QUANT, int MAXV>
+__global__ void __launch_bounds__(128, MAXV <= 8 ? 4 : 3) norm_row_keep_kernel(const NormArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int H = a.H;
+  const int NV = H >> 3;
+  const uint32_t row_bytes = (uint32_t)H * (uint32_t)sizeof(T);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * (size_t)row_bytes);
+  float* red = reinterpret_cast<float*>(bar + 2);
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  T* const xb = static_cast<T*>(a.x);
+  T* const rb = static_cast<T*>(a.r);
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar, 2 * row_bytes);
+    bulk_load(smem, xb + row * a.x_stride, row_bytes, bar);
+    bulk_load(smem + row_bytes, rb + row * a.r_stride, row_bytes, bar);
+  }
+  float inv_scale = 1.0f;
+  if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
+  Vec16 wv[MAXV];
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = tid + j * 128;
+    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+  }
+  const bool ok = mbar_wait_bounded(bar, 0);
+  const unsigned char* sx = smem;
+  const unsigned char* sr = smem + row_bytes;
+  float h[MAXV][8];
+  float ss = 0.f;
+  if (ok) {
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int v = tid + j * 128;
+      if (v < NV) {
+        float rf[8];
+        unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), h[j]);
+        unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          h[j][e] += rf[e];
+          ss += h[j][e] * h[j][e];
+        }
+        st_plain(rb + row * a.r_stride + (size_t)v * 8, pack8<T>(h[j]));
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) {
+      atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+      (void)mbar_wait_bounded(bar, 0);  // the copies may still be landing in this CTA's shared memory
+    }
+    pdl_launch_dependents();
+    return;
+  }
+  const float rstd = rsqrtf((red[0] + red[1] + red[2] + red[3]) * (1.0f / (float)H) + a.eps);
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = tid + j * 128;
+    if (v < NV) {
+      float y[8], wf[8];
+      unpack8<T>(wv[j], wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = h[j][e] * rstd * wf[e];
+      if constexpr (QUANT) {
+        uint2 q;
+        q.x = (uint32_t)f2_to_e4m3x2(y[0] * inv_scale, y[1] * inv_scale) |
+              ((uint32_t)f2_to_e4m3x2(y[2] * inv_scale, y[3] * inv_scale) << 16);
+        q.y = (uint32_t)f2_to_e4m3x2(y[4] * inv_scale, y[5] * inv_scale) |
+              ((uint32_t)f2_to_e4m3x2(y[6] * inv_scale, y[7] * inv_scale) << 16);
+        *reinterpret_cast<uint2*>(a.out + row * a.out_stride + (size_t)v * 8) = q;
+      } else {
+        st_plain(xb + row * a.x_stride + (size_t)v * 8, pack8<T>(y));
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
 // Persistent variant of the row-block kernel: grid = SMs x resident CTAs, CTA c handling row groups
 // c, c + grid, ... (rpc rows each, tpr threads per row). Thread 0 keeps S - 1 groups' bulk copies in
 // flight ahead of the one being computed, in an S-stage shared-memory ring (one mbarrier per stage);

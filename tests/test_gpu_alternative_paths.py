@@ -21,6 +21,7 @@ TESTS = Path(__file__).resolve().parent
 CASES = {
     "norm-loop": ({"MAS_NORM_IMPL": "loop"}, ["test_gpu_norm.py"]),
     "norm-row": ({"MAS_NORM_IMPL": "row"}, ["test_gpu_norm.py"]),
+    "norm-rowreg": ({"MAS_NORM_IMPL": "rowreg"}, ["test_gpu_norm.py"]),
     "norm-ring": ({"MAS_NORM_IMPL": "ring", "MAS_NORM_STAGES": "3"}, ["test_gpu_norm.py"]),
     "rope-ring": ({"MAS_ROPE_IMPL": "ring"}, ["test_gpu_rope.py", "test_gpu_llama4.py"]),
     "rope-vec": ({"MAS_ROPE_IMPL": "vec"}, ["test_gpu_rope.py", "test_gpu_llama4.py"]),
