@@ -81,8 +81,10 @@ def measured_peak() -> tuple[float, str]:
 # algorithmic bytes; writes come out lower because dirty lines still in the 126 MB L2 when the kernel
 # ends are not counted.
 NCU_TRAFFIC = {
-    "chain": (214_014_208 + 156_158_976, "profiles/norm_row_chain_shape.md"),
-    "norm_chain": (214_014_208 + 156_158_976, "profiles/norm_row_chain_shape.md"),
+    "chain": (214_000_896 + 157_683_968, "profiles/norm_row_keep_chain_shape.md"),
+    "norm_chain": (214_000_896 + 157_683_968, "profiles/norm_row_keep_chain_shape.md"),
+    "chain_fp8": (213_974_272 + 105_492_480, "profiles/norm_row_keep_chain_shape.md"),
+    "norm_fp8_chain": (213_974_272 + 105_492_480, "profiles/norm_row_keep_chain_shape.md"),
     "norm": (83_929_344 + 25_862_656, "profiles/norm_loop_config1.md"),
     "norm_fp8": (83_932_416 + 11_052_544, "profiles/ops_dram_traffic.md"),
     "silu": (1_073_793_792 + 484_039_168, "profiles/ops_dram_traffic.md"),
@@ -98,7 +100,7 @@ NCU_TRAFFIC = {
 # Mean device time of the dominant kernel inside the chain, from an ncu launch list of the bench's
 # own default command (gpu__time_duration.sum only, --clock-control none): an unperturbed in-chain
 # figure beside the event-bracketed one, which cancels the programmatic-launch overlap around it.
-NCU_IN_CHAIN = {"chain": (63.54, "profiles/chain_launches.md")}
+NCU_IN_CHAIN = {"chain": (62.24, "profiles/chain_launches.md")}
 
 # Bound on the end-to-end oracle check of sampled tokens (bf16 ulps / e4m3 steps after 88 layers).
 CHECK_BOUND_ULP = 8
