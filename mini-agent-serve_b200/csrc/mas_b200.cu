@@ -86,6 +86,8 @@ cudaError_t opt_in_norm_row() {
   if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 6>);
   if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 8>);
   if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 12>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 6, 256>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 3, 512>);
   return e;
 }
 
@@ -287,25 +289,32 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
       return launch(norm_loop_kernel<T, Q, 16>, g, b, smem, stream, pdl, a, tpr, rpc);
     }
   }
-  // Above H = 6144 (up to 12288) the register-resident row kernel, except for steps of at most one
-  // row per SM, where the row kernel with four times the threads per row is faster (2.9 against
-  // 3.0 us at 64 rows). At H = 12288: 4352 rows 65.6-65.7 us (row kernel 66.6-67.2, flashinfer
-  // 65.9-66.0), e4m3 out 57.5-57.6 us (60.0-60.3, flashinfer 70.1-70.8), 256 rows 4.0 us (4.3-4.5).
-  const bool rowreg_default = !use_ring && !use_row && !use_loop && H > 6144 && a.rows > (int64_t)st.sm_count;
+  // Above H = 6144 (up to 12288) the register-resident row kernel: one row of 128 threads per CTA,
+  // of 256 threads when a step has at most eight rows per SM, of 512 at most one. At H = 12288 in
+  // isolation: 4352 rows 65.6-65.7 us (the row kernel below 66.6-67.2, flashinfer 65.9-66.0), e4m3
+  // out 57.5-57.6 us (60.0-60.3, flashinfer 70.1-70.8). In a CUDA graph (row kernel / flashinfer in
+  // brackets): 64 rows 2.43 us (2.89 / 2.70), 256 rows 3.56 (4.5 / 4.55), 512 rows 6.3 (7.6 / 7.6),
+  // 1024 rows 11.1 (11.9 / 12.8); from about 2048 rows 128 threads are as fast or faster.
+  const bool rowreg_default = !use_ring && !use_row && !use_loop && H > 6144;
   if (fast_ok && H % 8 == 0 && (use_rowreg || rowreg_default) && H / 8 <= 12 * 128 && a.rows <= INT32_MAX) {
     const int nv = H / 8;
-    const size_t smem = 2 * (size_t)H * sizeof(T) + 16 + 4 * sizeof(float);
-    const dim3 g((unsigned)a.rows), b(128);
-    if (nv <= 4 * 128) return launch(norm_row_keep_kernel<T, Q, 4>, g, b, smem, stream, pdl, a);
-    if (nv <= 6 * 128) return launch(norm_row_keep_kernel<T, Q, 6>, g, b, smem, stream, pdl, a);
-    if (nv <= 8 * 128) return launch(norm_row_keep_kernel<T, Q, 8>, g, b, smem, stream, pdl, a);
-    return launch(norm_row_keep_kernel<T, Q, 12>, g, b, smem, stream, pdl, a);
+    static const int env_nt = env_int("MAS_NORM_KEEP_THREADS", 0);
+    int nt = a.rows <= (int64_t)st.sm_count ? 512 : a.rows <= 8 * (int64_t)st.sm_count ? 256 : 128;
+    if (env_nt == 128 || env_nt == 256 || env_nt == 512) nt = env_nt;
+    const size_t smem = 2 * (size_t)H * sizeof(T) + 16 + (size_t)(nt / 32) * sizeof(float);
+    const dim3 g((unsigned)a.rows), b(nt);
+    if (nt == 512 && nv <= 3 * 512) return launch(norm_row_keep_kernel<T, Q, 3, 512>, g, b, smem, stream, pdl, a);
+    if (nt == 256 && nv <= 6 * 256) return launch(norm_row_keep_kernel<T, Q, 6, 256>, g, b, smem, stream, pdl, a);
+    if (nv <= 4 * 128) return launch(norm_row_keep_kernel<T, Q, 4>, dim3((unsigned)a.rows), dim3(128), smem, stream, pdl, a);
+    if (nv <= 6 * 128) return launch(norm_row_keep_kernel<T, Q, 6>, dim3((unsigned)a.rows), dim3(128), smem, stream, pdl, a);
+    if (nv <= 8 * 128) return launch(norm_row_keep_kernel<T, Q, 8>, dim3((unsigned)a.rows), dim3(128), smem, stream, pdl, a);
+    return launch(norm_row_keep_kernel<T, Q, 12>, dim3((unsigned)a.rows), dim3(128), smem, stream, pdl, a);
   }
   if (fast_ok && H % 8 == 0 && !use_ring) {
-    // Row-block CTAs: threads per row grow with H (32 ... 256), 128 or 256 threads per CTA. A step
-    // with few rows (at most about one or three per SM) has too few CTAs to hide a row's latency, so
-    // its rows get four or two times the threads (at H = 12288 in a CUDA graph: 64 rows 3.7 -> 2.8 us,
-    // 256 rows 4.8 -> 4.3 us; from 512 rows up the base count is best).
+    // Row-block CTAs (H above 12288, or MAS_NORM_IMPL=row): threads per row grow with H (32 ... 256),
+    // 128 or 256 threads per CTA. A step with few rows (at most about one or three per SM) has too
+    // few CTAs to hide a row's latency, so its rows get four or two times the threads (at H = 12288
+    // in a CUDA graph: 64 rows 3.7 -> 2.8 us, 256 rows 4.8 -> 4.3 us).
     static const int env_tpr = env_int("MAS_NORM_TPR", 0);
     static const int env_cta = env_int("MAS_NORM_CTA_THREADS", 0);
     int tpr = H <= 3072 ? 32 : H <= 6144 ? 64 : H <= 16384 ? 128 : 256;

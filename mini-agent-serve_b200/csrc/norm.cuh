@@ -352,13 +352,13 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
   pdl_launch_dependents();
 }
 
-// Row-block variant that keeps h = x + r in registers between the two passes (one row of 128
-// threads per CTA, at most MAXV vectors per thread): the second pass needs no shared-memory re-read
-// and no re-unpacking, at the price of about 160 registers a thread at MAXV = 12 (3 CTAs per SM
-// instead of 4; the launch bounds hold the compiler to that, without them it took 178 registers and
-// fit only 2).
-template <typename T, bool QUANT, int MAXV>
-__global__ void __launch_bounds__(128, MAXV <= 8 ? 4 : 3) norm_row_keep_kernel(const NormArgs a) {
+// Row-block variant that keeps h = x + r in registers between the two passes (one row of NT threads
+// per CTA, at most MAXV vectors per thread): the second pass needs no shared-memory re-read and no
+// re-unpacking, at the price of about 160 registers a thread at MAXV = 12 (3 CTAs of 128 threads per
+// SM instead of 4; the launch bounds hold the compiler to that, without them it took 178 registers
+// and fit only 2). Steps with few rows use wider rows (NT = 256, 512) to spread each row's latency.
+template <typename T, bool QUANT, int MAXV, int NT = 128>
+__global__ void __launch_bounds__(NT, NT > 128 ? 1 : (MAXV <= 8 ? 4 : 3)) norm_row_keep_kernel(const NormArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int H = a.H;
   const int NV = H >> 3;
@@ -386,7 +386,7 @@ __global__ void __launch_bounds__(128, MAXV <= 8 ? 4 : 3) norm_row_keep_kernel(c
   Vec16 wv[MAXV];
 #pragma unroll
   for (int j = 0; j < MAXV; ++j) {
-    const int v = tid + j * 128;
+    const int v = tid + j * NT;
     if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
   }
   const bool ok = mbar_wait_bounded(bar, 0);
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(128, MAXV <= 8 ? 4 : 3) norm_row_keep_kernel(c
   if (ok) {
 #pragma unroll
     for (int j = 0; j < MAXV; ++j) {
-      const int v = tid + j * 128;
+      const int v = tid + j * NT;
       if (v < NV) {
         float rf[8];
         unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), h[j]);
@@ -421,10 +421,13 @@ __global__ void __launch_bounds__(128, MAXV <= 8 ? 4 : 3) norm_row_keep_kernel(c
     pdl_launch_dependents();
     return;
   }
-  const float rstd = rsqrtf((red[0] + red[1] + red[2] + red[3]) * (1.0f / (float)H) + a.eps);
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) tot += red[w];
+  const float rstd = rsqrtf(tot * (1.0f / (float)H) + a.eps);
 #pragma unroll
   for (int j = 0; j < MAXV; ++j) {
-    const int v = tid + j * 128;
+    const int v = tid + j * NT;
     if (v < NV) {
       float y[8], wf[8];
       unpack8<T>(wv[j], wf);
