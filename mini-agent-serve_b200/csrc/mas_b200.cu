@@ -88,6 +88,9 @@ cudaError_t opt_in_norm_row() {
   if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 12>);
   if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 6, 256>);
   if (e == cudaSuccess) e = opt_in_smem(norm_row_keep_kernel<T, Q, 3, 512>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_loop_keep_kernel<T, Q, 4, 128>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_loop_keep_kernel<T, Q, 4, 160>);
+  if (e == cudaSuccess) e = opt_in_smem(norm_loop_keep_kernel<T, Q, 4, 192>);
   return e;
 }
 
@@ -252,9 +255,40 @@ int run_norm(NormArgs a, const DeviceState& st, bool fast_ok, void* stream, int 
   static const bool use_row = env_is("MAS_NORM_IMPL", "row");
   static const bool use_loop = env_is("MAS_NORM_IMPL", "loop");
   static const bool use_rowreg = env_is("MAS_NORM_IMPL", "rowreg");
-  // Default: the persistent loop up to H = 6144 (config 1's H = 5120 measured 26.3 us against 29.5
-  // for the row-block grid), the register-resident row kernel above (below).
-  if (fast_ok && H % 8 == 0 && (use_loop || (!use_ring && !use_row && !use_rowreg && H <= 6144))) {
+  static const bool use_loopreg = env_is("MAS_NORM_IMPL", "loopreg");
+  const bool loopreg_default = !use_ring && !use_row && !use_loop && !use_rowreg;
+  if (fast_ok && H % 8 == 0 && (use_loopreg || loopreg_default) && H / 8 > 3 * 128 && H / 8 <= 4 * 192) {
+    // Default for 3072 < H <= 6144: the register-resident persistent loop (norm_loop_keep_kernel),
+    // one row of nt = H/32 threads (rounded up to a warp: 128, 160 or 192) per CTA and iteration, two
+    // stages. Configuration 1 (H = 5120, 4096 rows), against norm_loop_kernel's 26.8-27.0 us (bf16)
+    // and 25.8 us (e4m3 out): bf16 26.4-26.6 us at four CTAs per SM (within 1 % of every other
+    // stage / CTA count); e4m3 out 23.1-23.4 us at three CTAs per SM, against 25.0 at four and 27-28
+    // at two (three stages: 23.7-23.8).
+    static const int env_stages = env_int("MAS_NORM_STAGES", 0);
+    static const int env_ctas = env_int("MAS_NORM_CTAS_PER_SM", 0);
+    const int nt = (int)ceil_div(ceil_div(H / 8, 4), 32) * 32;
+    const int stages = std::max(2, std::min(8, env_stages > 0 ? env_stages : 2));
+    const size_t smem = norm_loop_keep_smem_bytes(H, stages, nt, (int)sizeof(T));
+    if (smem <= kMaxSmemPerCta) {
+      const void* fn = nt == 128 ? (const void*)norm_loop_keep_kernel<T, Q, 4, 128>
+                     : nt == 160 ? (const void*)norm_loop_keep_kernel<T, Q, 4, 160>
+                                 : (const void*)norm_loop_keep_kernel<T, Q, 4, 192>;
+      int ctas = resident_ctas(fn, nt, smem);
+      if (env_ctas > 0) ctas = std::min(ctas, env_ctas);
+      else if (Q) ctas = std::min(ctas, 3);
+      const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(a.rows, (int64_t)st.sm_count * std::max(1, ctas)));
+      a.stages = stages;
+      const dim3 g((unsigned)grid), b(nt);
+      if (nt == 128) return launch(norm_loop_keep_kernel<T, Q, 4, 128>, g, b, smem, stream, pdl, a);
+      if (nt == 160) return launch(norm_loop_keep_kernel<T, Q, 4, 160>, g, b, smem, stream, pdl, a);
+      return launch(norm_loop_keep_kernel<T, Q, 4, 192>, g, b, smem, stream, pdl, a);
+    }
+  }
+  // Default up to H = 3072 (and for any H up to 6144 that the loop above does not take): the
+  // persistent loop (at H = 5120 it measured 26.3 us against 29.5 for the row-block grid); the
+  // register-resident row kernel above H = 6144 (below).
+  if (fast_ok && H % 8 == 0 &&
+      (use_loop || (!use_ring && !use_row && !use_rowreg && H <= 6144))) {
     // Persistent row-group loop (norm_loop_kernel): S-stage ring, every thread a consumer. By
     // default at most 4 vectors per thread (threads per row = H/32, rounded up to a warp), CTAs of at
     // least 128 threads (one row each from 128 threads per row up) and two stages: at H = 5120, four

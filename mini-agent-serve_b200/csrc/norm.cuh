@@ -9,8 +9,12 @@
 // Fast paths (rows of H % 8 == 0 elements, 16-byte aligned rows), all staging whole rows of x and r
 // in shared memory with bulk copies (cp.async.bulk) and keeping the thread's weight slice in
 // registers:
-//   - norm_loop_kernel (the default up to H = 6144): a persistent grid; each CTA loops over row
+//   - norm_loop_kernel (the default up to H = 3072): a persistent grid; each CTA loops over row
 //     groups with the next group's copies in flight in a small ring, every thread a consumer;
+//   - norm_loop_keep_kernel (the default for 3072 < H <= 6144): the same loop with one row per CTA
+//     and iteration and h kept in registers, each stage refilled as soon as its first pass is done;
+//   - norm_row_keep_kernel (the default for 6144 < H <= 12288): one short-lived CTA per row, h kept
+//     in registers between the passes;
 //   - norm_row_kernel (the default above): one short-lived CTA per group of rows, one mbarrier;
 //   - norm_tma_kernel (selectable, and the path for rows too wide for the others): a persistent,
 //     warp-specialised ring. Warp 0's first lane streams rows into an S-stage ring (`full`
@@ -583,6 +587,135 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_loop_kernel(const Nor
     for (int m = 0; m < S; ++m) {
       const int64_t gm = g0 + (int64_t)(k + m) * gstep;
       if (gm < ngroups) (void)mbar_wait_bounded(&bar[(k + m) % S], (uint32_t)((k + m) / S) & 1u);
+    }
+  }
+  pdl_launch_dependents();
+}
+
+// Persistent loop that keeps h = x + r in registers (one row of NT threads per CTA and iteration, at
+// most MAXV vectors per thread). Once the first pass has read a stage, that stage is no longer needed:
+// thread 0 refills it right after the reduction barrier, so the next copy is in flight while the
+// second pass runs from registers, and no barrier closes the iteration (the reduction slots are
+// double-buffered by iteration parity instead).
+__host__ __device__ inline size_t norm_loop_keep_smem_bytes(int H, int stages, int nt, int elem_bytes) {
+  return (size_t)stages * 2 * (size_t)H * (size_t)elem_bytes + (size_t)stages * 8 +
+         2 * (size_t)(nt / 32) * sizeof(float);
+}
+
+template <typename T, bool QUANT, int MAXV, int NT>
+__global__ void __launch_bounds__(NT, 4) norm_loop_keep_kernel(const NormArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int H = a.H;
+  const int NV = H >> 3;
+  const int S = a.stages;
+  const uint32_t row_bytes = (uint32_t)H * (uint32_t)sizeof(T);
+  const size_t stage_bytes = 2 * (size_t)row_bytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  float* red = reinterpret_cast<float*>(bar + S);
+  const int tid = threadIdx.x;
+  const int64_t g0 = blockIdx.x, gstep = gridDim.x;
+
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  T* const xb = static_cast<T*>(a.x);
+  T* const rb = static_cast<T*>(a.r);
+  auto issue = [&](int64_t row, int s) {
+    unsigned char* st = smem + (size_t)s * stage_bytes;
+    mbar_arrive_expect_tx(&bar[s], 2 * row_bytes);
+    bulk_load(st, xb + row * a.x_stride, row_bytes, &bar[s]);
+    bulk_load(st + row_bytes, rb + row * a.r_stride, row_bytes, &bar[s]);
+  };
+  if (tid == 0) {
+    for (int k = 0; k < S; ++k) {
+      const int64_t row = g0 + (int64_t)k * gstep;
+      if (row < a.rows) issue(row, k);
+    }
+  }
+  float inv_scale = 1.0f;
+  if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
+  Vec16 wv[MAXV];
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = tid + j * NT;
+    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+  }
+
+  int k = 0;
+  bool timed_out = false;
+  for (int64_t row = g0; row < a.rows; row += gstep, ++k) {
+    const int s = k % S;
+    const bool ok = mbar_wait_bounded(&bar[s], (uint32_t)(k / S) & 1u);
+    const unsigned char* sx = smem + (size_t)s * stage_bytes;
+    const unsigned char* sr = sx + row_bytes;
+    float h[MAXV][8];
+    float ss = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int j = 0; j < MAXV; ++j) {
+        const int v = tid + j * NT;
+        if (v < NV) {
+          float rf[8];
+          unpack8<T>(*reinterpret_cast<const Vec16*>(sx + (size_t)v * 16), h[j]);
+          unpack8<T>(*reinterpret_cast<const Vec16*>(sr + (size_t)v * 16), rf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            h[j][e] += rf[e];
+            ss += h[j][e] * h[j][e];
+          }
+          st_plain(rb + row * a.r_stride + (size_t)v * 8, pack8<T>(h[j]));
+        }
+      }
+    }
+    ss = warp_sum(ss);
+    float* rk = red + (k & 1) * (NT / 32);
+    if ((tid & 31) == 0) rk[tid >> 5] = ss;
+    if (__syncthreads_or(!ok)) {
+      timed_out = true;
+      break;
+    }
+    if (tid == 0) {  // every thread has read stage s: refill it with the row S iterations ahead
+      const int64_t rn = row + (int64_t)S * gstep;
+      if (rn < a.rows) {
+        fence_proxy_async_smem();
+        issue(rn, s);
+      }
+    }
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) tot += rk[w];
+    const float rstd = rsqrtf(tot * (1.0f / (float)H) + a.eps);
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+      const int v = tid + j * NT;
+      if (v < NV) {
+        float y[8], wf[8];
+        unpack8<T>(wv[j], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) y[e] = h[j][e] * rstd * wf[e];
+        if constexpr (QUANT) {
+          uint2 q;
+          q.x = (uint32_t)f2_to_e4m3x2(y[0] * inv_scale, y[1] * inv_scale) |
+                ((uint32_t)f2_to_e4m3x2(y[2] * inv_scale, y[3] * inv_scale) << 16);
+          q.y = (uint32_t)f2_to_e4m3x2(y[4] * inv_scale, y[5] * inv_scale) |
+                ((uint32_t)f2_to_e4m3x2(y[6] * inv_scale, y[7] * inv_scale) << 16);
+          *reinterpret_cast<uint2*>(a.out + row * a.out_stride + (size_t)v * 8) = q;
+        } else {
+          st_plain(xb + row * a.x_stride + (size_t)v * 8, pack8<T>(y));
+        }
+      }
+    }
+  }
+  if (timed_out && tid == 0) {
+    // Iteration k's wait gave up: the fills of iterations k .. k + S - 1 may still be landing in this
+    // CTA's shared memory. Wait for each (bounded) before the CTA exits.
+    atomicOr(a.fault, MAS_STATUS_COPY_TIMEOUT);
+    for (int m = 0; m < S; ++m) {
+      const int64_t rm = g0 + (int64_t)(k + m) * gstep;
+      if (rm < a.rows) (void)mbar_wait_bounded(&bar[(k + m) % S], (uint32_t)((k + m) / S) & 1u);
     }
   }
   pdl_launch_dependents();

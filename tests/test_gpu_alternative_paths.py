@@ -1,7 +1,7 @@
 """The non-default kernels of each op, through the same parity tests as the defaults.
 
 Each op picks among several kernels by shape and step size (and the choice can be forced from the
-environment, read once per process: MAS_NORM_IMPL, MAS_NORM_KEEP_THREADS, MAS_ROPE_IMPL, MAS_SILU_IMPL,
+environment, read once per process: MAS_NORM_IMPL, MAS_NORM_STAGES, MAS_NORM_KEEP_THREADS, MAS_ROPE_IMPL, MAS_SILU_IMPL,
 MAS_EMBED_IMPL).
 A choice the default shapes never reach would otherwise go untested, so every forced choice reruns
 its op's test files in a child process with the variable set.
@@ -21,6 +21,7 @@ TESTS = Path(__file__).resolve().parent
 
 CASES = {
     "norm-loop": ({"MAS_NORM_IMPL": "loop"}, ["test_gpu_norm.py"]),
+    "norm-loopreg-3stages": ({"MAS_NORM_IMPL": "loopreg", "MAS_NORM_STAGES": "3"}, ["test_gpu_norm.py"]),
     "norm-row": ({"MAS_NORM_IMPL": "row"}, ["test_gpu_norm.py"]),
     "norm-rowreg": ({"MAS_NORM_IMPL": "rowreg"}, ["test_gpu_norm.py"]),
     "norm-rowreg-256": ({"MAS_NORM_IMPL": "rowreg", "MAS_NORM_KEEP_THREADS": "256"}, ["test_gpu_norm.py"]),

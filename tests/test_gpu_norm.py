@@ -39,6 +39,7 @@ def _run_bf16(cuda, T, H, dtype=torch.bfloat16, stride=None, eps=1e-5, rscale=1.
 
 
 @pytest.mark.parametrize("T,H", [(1, 5120), (7, 5120), (33, 12288), (5, 1000), (300, 4096), (2, 16384),
+                                 (9, 6144), (700, 3200), (1000, 5632),
                                  (3, 24576), (64, 128), (9, 8)])
 def test_norm_fast_path(cuda, T, H):
     _run_bf16(cuda, T, H)
@@ -91,7 +92,7 @@ def test_norm_repeat_deterministic(cuda):
 
 
 @pytest.mark.parametrize("T,H,scale", [(6, 5120, 0.05), (3, 12288, 0.005), (4, 1000, 0.5), (5, 1001, 0.05),
-                                       (2, 32768, 0.05), (1, 8, 1.0)])
+                                       (2, 32768, 0.05), (1, 8, 1.0), (1000, 5632, 0.05), (700, 3200, 0.02)])
 def test_norm_quant(cuda, T, H, scale):
     xb, rb, w = _inputs(T, H, torch.bfloat16)
     out = torch.empty(T, H, dtype=torch.float8_e4m3fn, device=cuda)
