@@ -461,6 +461,8 @@ int launch_rope_ring_t(RopeRingArgs r, bool bf, bool i64, bool neox, DeviceState
   r.stages = stages;
   static const int env_early = env_int("MAS_ROPE_EARLY_DEPENDENTS", 0);
   r.early_dependents = env_early > 0 ? 1 : 0;
+  static const int env_prefetch = env_int("MAS_ROPE_PREFETCH_QK", 1);
+  r.prefetch_qk = env_prefetch > 0 ? 1 : 0;
   const size_t smem = rope_ring_smem_bytes(stage, stages, r.tokens_per_cta, APPEND);
   const dim3 g((unsigned)grid), b(threads);
   if (bf) {

@@ -234,6 +234,7 @@ struct RopeRingArgs {
   int64_t vsn;
   PagedKVArgs kv;
   int32_t early_dependents;  // signal programmatic dependents after the prologue instead of at the end
+  int32_t prefetch_qk;       // start the first stages' q/k copies before the positions are staged
 };
 
 constexpr int kRopeConsumerWarps = 8;        // default consumer warps per CTA
@@ -275,7 +276,23 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
     }
     fence_barrier_init();
   }
+  __syncthreads();
   pdl_wait();
+  T* const qb = static_cast<T*>(a.q);
+  T* const kb = static_cast<T*>(a.k);
+  // A token's q and k rows do not depend on its position: the producer lane starts the first
+  // stages' q/k copies (expected bytes raised, no arrival yet) before the positions are read and
+  // staged; the cos|sin row (and v) and the stage's one arrival follow in the loop below.
+  const int pre = a.prefetch_qk ? min(n, S) : 0;
+  if (tid == 0) {
+    for (int i = 0; i < pre; ++i) {
+      unsigned char* st = smem + (size_t)i * stage_bytes;
+      const int64_t t = tok0 + i;
+      mbar_expect_tx(&full[i], q_bytes + k_bytes);
+      if (q_bytes) bulk_load(st, qb + t * a.qsn, q_bytes, &full[i]);
+      if (k_bytes) bulk_load(st + q_bytes, kb + t * a.ksn, k_bytes, &full[i]);
+    }
+  }
   const PosT* pos_p = static_cast<const PosT*>(a.pos) + tok0;
   for (int i = tid; i < n; i += blockDim.x) {
     const int64_t pos = (int64_t)pos_p[i];
@@ -297,8 +314,6 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
   // for this whole grid to finish.
   if (a.early_dependents) pdl_launch_dependents();
 
-  T* const qb = static_cast<T*>(a.q);
-  T* const kb = static_cast<T*>(a.k);
   int issued = 0;     // producer lane: tokens whose stage has been filled (or marked empty)
   bool gave_up = false;  // this thread's bounded wait ran out
   if (warp == 0) {
@@ -312,16 +327,19 @@ __global__ void __launch_bounds__(kRopeRingMaxThreads) rope_ring_kernel(const Ro
         }
         issued = i + 1;
         const int64_t pos = spos[i];
-        if (pos < 0) {
+        if (pos < 0) {  // (prefetched q/k still land before the phase completes)
           mbar_arrive(&full[s]);
           continue;
         }
         unsigned char* st = smem + (size_t)s * stage_bytes;
         const int64_t t = tok0 + i;
         const bool with_v = APPEND && v_bytes != 0u && sslot[i] >= 0;
-        mbar_arrive_expect_tx(&full[s], stage_bytes - (with_v ? 0u : v_bytes));
-        if (q_bytes) bulk_load(st, qb + t * a.qsn, q_bytes, &full[s]);
-        if (k_bytes) bulk_load(st + q_bytes, kb + t * a.ksn, k_bytes, &full[s]);
+        const bool qk_in_flight = i < pre;
+        mbar_arrive_expect_tx(&full[s], c_bytes + (with_v ? v_bytes : 0u) + (qk_in_flight ? 0u : q_bytes + k_bytes));
+        if (!qk_in_flight) {
+          if (q_bytes) bulk_load(st, qb + t * a.qsn, q_bytes, &full[s]);
+          if (k_bytes) bulk_load(st + q_bytes, kb + t * a.ksn, k_bytes, &full[s]);
+        }
         if (with_v) bulk_load(st + q_bytes + k_bytes, static_cast<const T*>(a.v) + t * a.vsn, v_bytes, &full[s]);
         bulk_load(st + q_bytes + k_bytes + v_bytes, a.cache + pos * a.rd, c_bytes, &full[s]);
       }

@@ -1,7 +1,8 @@
 """The non-default kernels of each op, through the same parity tests as the defaults.
 
 Each op picks among several kernels by shape and step size (and the choice can be forced from the
-environment, read once per process: MAS_NORM_IMPL, MAS_NORM_STAGES, MAS_NORM_KEEP_THREADS, MAS_ROPE_IMPL, MAS_SILU_IMPL,
+environment, read once per process: MAS_NORM_IMPL, MAS_NORM_STAGES, MAS_NORM_KEEP_THREADS, MAS_ROPE_IMPL,
+MAS_ROPE_PREFETCH_QK, MAS_SILU_IMPL,
 MAS_EMBED_IMPL).
 A choice the default shapes never reach would otherwise go untested, so every forced choice reruns
 its op's test files in a child process with the variable set.
@@ -28,6 +29,8 @@ CASES = {
     "norm-rowreg-512": ({"MAS_NORM_IMPL": "rowreg", "MAS_NORM_KEEP_THREADS": "512"}, ["test_gpu_norm.py"]),
     "norm-ring": ({"MAS_NORM_IMPL": "ring", "MAS_NORM_STAGES": "3"}, ["test_gpu_norm.py"]),
     "rope-ring": ({"MAS_ROPE_IMPL": "ring"}, ["test_gpu_rope.py", "test_gpu_llama4.py"]),
+    "rope-ring-no-prefetch": ({"MAS_ROPE_IMPL": "ring", "MAS_ROPE_PREFETCH_QK": "0"},
+                              ["test_gpu_rope.py", "test_gpu_paged_kv.py"]),
     "rope-vec": ({"MAS_ROPE_IMPL": "vec"}, ["test_gpu_rope.py", "test_gpu_llama4.py"]),
     "silu-ring": ({"MAS_SILU_IMPL": "ring"}, ["test_gpu_silu.py", "test_gpu_silu_quant.py"]),
     "embed-tma": ({"MAS_EMBED_IMPL": "tma"}, ["test_gpu_embed.py"]),
