@@ -126,16 +126,10 @@ __device__ __forceinline__ float2 fma2_f32(float2 a, float2 b, float2 c) {
 // ---------------------------------------------------------------------------------------------
 // Global memory access.
 // ---------------------------------------------------------------------------------------------
-// Read-only streaming load: not kept in L1 (each byte is read once).
-__device__ __forceinline__ Vec16 ld_stream(const void* p) {
-  Vec16 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.a), "=r"(v.b), "=r"(v.c), "=r"(v.d)
-               : "l"(p));
-  return v;
-}
-// Read-only load that may stay in L1 (reused data: weights, cos/sin rows).
-__device__ __forceinline__ Vec16 ld_cached(const void* p) {
+// Read-only 16-byte load through the non-coherent path, for data no kernel writes while this one
+// runs (inputs read once, weights, cos/sin rows). Without an L1 hint: L1::no_allocate on the streaming
+// reads of SiLU-mul measured 3 % slower (233.6 against 226.6 us for an [8192, 65536] input).
+__device__ __forceinline__ Vec16 ld_ro(const void* p) {
   Vec16 v;
   asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
                : "=r"(v.a), "=r"(v.b), "=r"(v.c), "=r"(v.d)

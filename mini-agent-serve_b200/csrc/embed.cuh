@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(kEmbedVecThreads) embed_vec_kernel(const Embed
 #pragma unroll
   for (int j = 0; j < kEmbedVecPerThread; ++j) {
     const uint32_t u = v0 + (uint32_t)j * kEmbedVecThreads;
-    if (u < b1) v[j] = valid ? ld_stream(src + (size_t)u * 16) : Vec16{0u, 0u, 0u, 0u};
+    if (u < b1) v[j] = valid ? ld_ro(src + (size_t)u * 16) : Vec16{0u, 0u, 0u, 0u};
   }
 #pragma unroll
   for (int j = 0; j < kEmbedVecPerThread; ++j) {
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(256) embed_generic_kernel(const EmbedArgs a, i
       const size_t off = (size_t)i * unit;
       switch (unit) {
         case 16: {
-          const Vec16 v = valid ? ld_stream(src + off) : Vec16{0u, 0u, 0u, 0u};
+          const Vec16 v = valid ? ld_ro(src + off) : Vec16{0u, 0u, 0u, 0u};
           st_plain(dst + off, v);
           break;
         }

@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(32 + kNormMaxConsumers) norm_tma_kernel(const 
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int v = ct + j * gsize;
-      if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+      if (v < NV) wv[j] = ld_ro(static_cast<const T*>(a.w) + (size_t)v * 8);
     }
     float inv_scale = 1.0f;
     if constexpr (QUANT) inv_scale = 1.0f / __ldg(a.scale);
@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_row_kernel(const Norm
 #pragma unroll
   for (int j = 0; j < MAXV; ++j) {
     const int v = rt + j * tpr;
-    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+    if (v < NV) wv[j] = ld_ro(static_cast<const T*>(a.w) + (size_t)v * 8);
   }
   const bool ok = mbar_wait_bounded(bar, 0);
   const bool active = rr < nrows;
@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(NT, NT > 128 ? 1 : (MAXV <= 8 ? 4 : 3)) norm_r
 #pragma unroll
   for (int j = 0; j < MAXV; ++j) {
     const int v = tid + j * NT;
-    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+    if (v < NV) wv[j] = ld_ro(static_cast<const T*>(a.w) + (size_t)v * 8);
   }
   const bool ok = mbar_wait_bounded(bar, 0);
   const unsigned char* sx = smem;
@@ -508,7 +508,7 @@ __global__ void __launch_bounds__(kNormRowMaxThreads) norm_loop_kernel(const Nor
 #pragma unroll
   for (int j = 0; j < MAXV; ++j) {
     const int v = rt + j * tpr;
-    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+    if (v < NV) wv[j] = ld_ro(static_cast<const T*>(a.w) + (size_t)v * 8);
   }
 
   int k = 0;
@@ -641,7 +641,7 @@ __global__ void __launch_bounds__(NT, 4) norm_loop_keep_kernel(const NormArgs a)
 #pragma unroll
   for (int j = 0; j < MAXV; ++j) {
     const int v = tid + j * NT;
-    if (v < NV) wv[j] = ld_cached(static_cast<const T*>(a.w) + (size_t)v * 8);
+    if (v < NV) wv[j] = ld_ro(static_cast<const T*>(a.w) + (size_t)v * 8);
   }
 
   int k = 0;

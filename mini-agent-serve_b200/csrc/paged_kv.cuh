@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(kAppendThreads) append_kv_vec_kernel(const App
       const T* src = static_cast<const T*>(is_v ? a.v : a.k) + t * (is_v ? a.vsn : a.ksn) +
                      (int64_t)h * (is_v ? a.vsh : a.ksh) + j * 8;
       T* dst = static_cast<T*>(is_v ? a.kv.v_cache : a.kv.k_cache) + slot + (int64_t)h * a.kv.stride_head + j * 8;
-      st_plain(dst, ld_stream(src));
+      st_plain(dst, ld_ro(src));
     }
   }
   pdl_launch_dependents();

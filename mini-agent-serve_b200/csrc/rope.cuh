@@ -44,8 +44,8 @@ struct RopeArgs {
 constexpr int kRopeThreads = 256;
 
 __device__ __forceinline__ void load_f8(const float* p, float (&f)[8]) {
-  const Vec16 a = ld_cached(p);
-  const Vec16 b = ld_cached(p + 4);
+  const Vec16 a = ld_ro(p);
+  const Vec16 b = ld_ro(p + 4);
   f[0] = __uint_as_float(a.a); f[1] = __uint_as_float(a.b);
   f[2] = __uint_as_float(a.c); f[3] = __uint_as_float(a.d);
   f[4] = __uint_as_float(b.a); f[5] = __uint_as_float(b.b);

@@ -225,8 +225,8 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
   if (v < nvec) {
     for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
       const T* g = static_cast<const T*>(a.in) + row * a.in_stride + (size_t)v * 8;
-      const Vec16 gv = ld_stream(g);
-      const Vec16 uv = ld_stream(g + a.d);
+      const Vec16 gv = ld_ro(g);
+      const Vec16 uv = ld_ro(g + a.d);
       float gf[8], uf[8], y[8];
       unpack8<T>(gv, gf);
       unpack8<T>(uv, uf);
