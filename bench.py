@@ -87,12 +87,13 @@ NCU_TRAFFIC = {
     "norm_fp8_chain": (213_974_272 + 105_492_480, "profiles/norm_row_keep_chain_shape.md"),
     "norm": (83_919_616 + 24_468_480, "profiles/norm_loop_keep_config1.md"),
     "norm_fp8": (83_921_152 + 10_962_688, "profiles/norm_loop_keep_config1.md"),
-    "silu": (1_073_793_792 + 484_039_168, "profiles/ops_dram_traffic.md"),
-    "silu_fp8": (1_073_780_224 + 218_833_920, "profiles/ops_dram_traffic.md"),
-    "embed": (164_091_392 + 110_841_088, "profiles/ops_dram_traffic.md"),
-    "rope": (328_030_464 + 254_389_504, "profiles/ops_dram_traffic.md"),
+    "silu": (1_073_837_568 + 498_061_312, "profiles/ops_dram_traffic.md"),
+    "silu_fp8": (1_073_865_728 + 253_526_784, "profiles/ops_dram_traffic.md"),
+    "silu_chain": (499_155_200 + 219_000_064, "profiles/ops_dram_traffic.md"),
+    "embed": (160_659_200 + 115_822_848, "profiles/ops_dram_traffic.md"),
+    "rope": (327_856_384 + 256_022_016, "profiles/ops_dram_traffic.md"),
     "rope_chain": (118_173_952 + 59_143_424, "profiles/rope_ring_chain_shape.md"),
-    "silu_fp8_chain": (499_213_568 + 75_594_752, "profiles/silu_fp8_chain_shape.md"),
+    "silu_fp8_chain": (499_176_448 + 109_594_624, "profiles/ops_dram_traffic.md"),
     "rope_append_small": (383_225_088 + 380_423_424, "profiles/ops_dram_traffic.md"),
 }
 
