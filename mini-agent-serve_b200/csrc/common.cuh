@@ -136,6 +136,15 @@ __device__ __forceinline__ Vec16 ld_ro(const void* p) {
                : "l"(p));
   return v;
 }
+// Read-only 16-byte load that allocates no L1 line (SiLU-mul's loads when its data may partly come
+// from L2: a 512-token step of an 88-layer chain 3.27 ms against 3.73 with ld_ro).
+__device__ __forceinline__ Vec16 ld_ro_noalloc(const void* p) {
+  Vec16 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.a), "=r"(v.b), "=r"(v.c), "=r"(v.d)
+               : "l"(p));
+  return v;
+}
 // Plain coherent 16-byte load (data this kernel also writes).
 __device__ __forceinline__ Vec16 ld_plain(const void* p) {
   Vec16 v;

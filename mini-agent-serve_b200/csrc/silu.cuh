@@ -209,7 +209,7 @@ __device__ __forceinline__ uint32_t quant4_e4m3_fast(const float* act, const Qua
 // registers, so 2048 threads per SM keep 64 KB of loads in flight; a 2-D grid of (256-vector column
 // blocks, row groups), each thread walking the rows of its group. QUANT writes 8 e4m3 bytes per
 // thread instead of 8 activations.
-template <typename T, bool QUANT>
+template <typename T, bool QUANT, bool NOALLOC = false>
 __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const SiluArgs a) {
   pdl_wait();
   const int nvec = a.d >> 3;
@@ -225,8 +225,8 @@ __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const Sil
   if (v < nvec) {
     for (int64_t row = blockIdx.y; row < a.rows; row += gridDim.y) {
       const T* g = static_cast<const T*>(a.in) + row * a.in_stride + (size_t)v * 8;
-      const Vec16 gv = ld_ro(g);
-      const Vec16 uv = ld_ro(g + a.d);
+      const Vec16 gv = NOALLOC ? ld_ro_noalloc(g) : ld_ro(g);
+      const Vec16 uv = NOALLOC ? ld_ro_noalloc(g + a.d) : ld_ro(g + a.d);
       float gf[8], uf[8], y[8];
       unpack8<T>(gv, gf);
       unpack8<T>(uv, uf);
