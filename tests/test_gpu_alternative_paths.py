@@ -2,7 +2,7 @@
 
 Each op picks among several kernels by shape and step size (and the choice can be forced from the
 environment, read once per process: MAS_NORM_IMPL, MAS_NORM_STAGES, MAS_NORM_KEEP_THREADS, MAS_ROPE_IMPL,
-MAS_ROPE_PREFETCH_QK, MAS_SILU_IMPL,
+MAS_ROPE_PREFETCH_QK, MAS_SILU_IMPL, MAS_SILU_NOALLOC,
 MAS_EMBED_IMPL).
 A choice the default shapes never reach would otherwise go untested, so every forced choice reruns
 its op's test files in a child process with the variable set.
@@ -33,6 +33,8 @@ CASES = {
                               ["test_gpu_rope.py", "test_gpu_paged_kv.py"]),
     "rope-vec": ({"MAS_ROPE_IMPL": "vec"}, ["test_gpu_rope.py", "test_gpu_llama4.py"]),
     "silu-ring": ({"MAS_SILU_IMPL": "ring"}, ["test_gpu_silu.py", "test_gpu_silu_quant.py"]),
+    "silu-loads-noalloc": ({"MAS_SILU_NOALLOC": "1"}, ["test_gpu_silu.py", "test_gpu_silu_quant.py"]),
+    "silu-loads-plain": ({"MAS_SILU_NOALLOC": "0"}, ["test_gpu_silu.py", "test_gpu_silu_quant.py"]),
     "embed-tma": ({"MAS_EMBED_IMPL": "tma"}, ["test_gpu_embed.py"]),
 }
 
