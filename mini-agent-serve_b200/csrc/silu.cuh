@@ -208,7 +208,8 @@ __device__ __forceinline__ uint32_t quant4_e4m3_fast(const float* act, const Qua
 // Register variant (the default fast path): one 16-byte gate/up pair per thread and row, 32
 // registers, so 2048 threads per SM keep 64 KB of loads in flight; a 2-D grid of (256-vector column
 // blocks, row groups), each thread walking the rows of its group. QUANT writes 8 e4m3 bytes per
-// thread instead of 8 activations.
+// thread instead of 8 activations. NOALLOC loads gate/up with L1::no_allocate (the host picks it for
+// launches whose data fit in about two L2s, plain read-only loads for those that stream from HBM).
 template <typename T, bool QUANT, bool NOALLOC = false>
 __global__ void __launch_bounds__(kSiluThreads, 8) silu_mul_vec_kernel(const SiluArgs a) {
   pdl_wait();
