@@ -76,3 +76,41 @@ def test_copies_go_to_the_threads_with_fewest_heads():
     copy_threads = {ncons - 1 - u for u in range(128)}
     assert max(per_thread[ct] for ct in copy_threads) == 1
     assert max(per_thread.values()) == 2
+
+
+def stage_accounting(pos_valid: bool, with_v: bool, prefetched: bool, q: int, k: int, v: int, c: int):
+    """One stage phase of the rope ring (rope.cuh, rope_ring_kernel), following the kernel's statements:
+    returns (bytes the barrier expects, bytes of the copies issued into the stage, arrivals). A
+    prefetched token's q/k copies start with expect_tx before the positions are staged; the
+    producer's loop then adds the cos|sin row (and v) with its one arrive.expect_tx, or arrives alone
+    for a token whose position is out of range."""
+    expect = []   # arguments of expect_tx / arrive.expect_tx
+    copies = []   # sizes of the bulk copies issued
+    arrivals = 0
+    if prefetched:                       # prologue: mbar_expect_tx(q + k); q, k copies
+        expect.append(q + k)
+        copies += [b for b in (q, k) if b]
+    if not pos_valid:                    # loop: pos < 0 -> mbar_arrive
+        arrivals += 1
+        return sum(expect), sum(copies), arrivals
+    qk_in_flight = prefetched            # loop: arrive.expect_tx(c + v? + (q + k unless in flight))
+    expect.append(c + (v if with_v else 0) + (0 if qk_in_flight else q + k))
+    arrivals += 1
+    if not qk_in_flight:
+        copies += [b for b in (q, k) if b]
+    if with_v:
+        copies.append(v)
+    copies.append(c)
+    return sum(expect), sum(copies), arrivals
+
+
+@pytest.mark.parametrize("shape", [(32 * 256, 8 * 256, 0, 512), (96 * 256, 8 * 256, 0, 512),
+                                   (32 * 256, 8 * 256, 8 * 256, 512), (0, 8 * 256, 8 * 256, 256)])
+def test_rope_stage_transaction_bytes_balance(shape):
+    q, k, v, c = shape
+    for pos_valid in (True, False):
+        for with_v in ((True, False) if v else (False,)):
+            for prefetched in (True, False):
+                expected, copied, arrivals = stage_accounting(pos_valid, with_v, prefetched, q, k, v, c)
+                assert expected == copied and arrivals == 1
+                assert expected < (1 << 20)  # an mbarrier's transaction count holds under 2^20 bytes
