@@ -10,7 +10,8 @@ vector exactly once. With `ncons` consumer threads and `tpu` = rotary_dim / 16 g
   ncons - 1 - ct, 2 * ncons - 1 - ct, ...
 
 The GPU tests check the results; this checks the index arithmetic over launch shapes they do not
-reach (other consumer-warp counts, rotary_dims and head counts).
+reach (other consumer-warp counts, rotary_dims and head counts), and that every stage phase expects
+exactly the bytes its copies deliver, with one arrival, in each way a token can be staged.
 """
 from __future__ import annotations
 
