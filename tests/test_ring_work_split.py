@@ -115,3 +115,15 @@ def test_rope_stage_transaction_bytes_balance(shape):
                 expected, copied, arrivals = stage_accounting(pos_valid, with_v, prefetched, q, k, v, c)
                 assert expected == copied and arrivals == 1
                 assert expected < (1 << 20)  # an mbarrier's transaction count holds under 2^20 bytes
+
+
+def test_drain_waits_on_the_last_copy_into_each_stage():
+    # common.cuh drain_ring: after `issued` loads into stages i % S, stage s (s < issued) is waited on
+    # for the phase of load k = s + ((issued - 1 - s) // S) * S with parity (k // S) & 1. That must be
+    # the last load into stage s (phases complete in order, so it covers the earlier ones).
+    for stages in range(1, 9):
+        for issued in range(0, 40):
+            for s in range(min(stages, issued)):
+                k = s + ((issued - 1 - s) // stages) * stages
+                last = max(i for i in range(issued) if i % stages == s)
+                assert k == last and k // stages == sum(1 for i in range(issued) if i % stages == s) - 1
